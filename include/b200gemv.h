@@ -1,0 +1,223 @@
+/*
+ * b200gemv.h -- C ABI of the B200 (sm_100a) decode-GEMV library for the
+ * Llama-3.2-3B MLP projections (gate/up 3072->8192, down 8192->3072, M=1..8).
+ *
+ * This is the drop-in boundary.  The reference project
+ * (sudb97/Llama-3.2-3B-Instruct-gemm-optimization) has no plugin code yet --
+ * plugin/ holds only .gitkeep and the IPluginV3 is an open TODO (TODO.md:69-70)
+ * -- so its operator surface is the in-file host API of kernels/gemv_fp8.cu and
+ * kernels/gemv_fp16.cu, plus the plugin-creator fields it planned
+ * (tensorrt_custom_tactic_kernel_b07f17a4.plan.md:57-58).  Each entry point
+ * below names the reference interface it replaces.
+ *
+ * Conventions (all entry points):
+ *  - The caller owns every device buffer; ops own host metadata only.
+ *  - Work is stream-ordered on the given cudaStream_t; no entry point that
+ *    takes a stream synchronises the host.
+ *  - Errors are returned as b2g_status, never by exit() (the reference calls
+ *    exit(1) from CHECK_CUDA, kernels/gemv_fp8.cu:38-46, and on an
+ *    unsupported N, :270-273).
+ *  - Weights are [K, N] row-major ("KN", the reference layout,
+ *    kernels/gemv_fp8.cu:93) or [N, K] ("NK", nn.Linear); activations x are
+ *    [m, K] fp16 with a row stride; outputs y are [m, N] fp16.
+ */
+#ifndef B200GEMV_H_
+#define B200GEMV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* b2g_stream_t; /* == cudaStream_t */
+
+typedef enum {
+  B2G_OK = 0,
+  B2G_ERR_INVALID = 1,      /* bad argument (null pointer, size, alignment) */
+  B2G_ERR_UNSUPPORTED = 2,  /* valid request this build does not implement */
+  B2G_ERR_CUDA = 3,         /* a CUDA runtime call failed */
+  B2G_ERR_PEER_TIMEOUT = 4, /* a device-side wait on a peer gave up */
+  B2G_ERR_OOM = 5,          /* shared memory or workspace too small */
+  B2G_ERR_DEVICE = 6        /* a kernel recorded an error (bounded wait expired) */
+} b2g_status;
+
+/* Weight element type (reference: FP16 kernels/gemv_fp16.cu, E4M3 kernels/gemv_fp8.cu). */
+enum { B2G_DTYPE_FP16 = 0, B2G_DTYPE_FP8_E4M3 = 1 };
+
+/* Scale modes.  NONE, TENSOR_FP16 and CHANNEL_FP16 are the reference's
+ * ScaleMode {kScaleNone, kScaleTensor, kScaleChannel} (kernels/gemv_fp8.cu:459)
+ * with fp16 scales (:515-540); CHANNEL_FP32 is the per-output-channel FP32
+ * absmax/448 rule.  Scales multiply the fp32 accumulator in the epilogue
+ * (the reference's cast_scale_f32_to_f16_kernel, kernels/gemv_fp8.cu:164-173). */
+enum {
+  B2G_SCALE_NONE = 0,
+  B2G_SCALE_TENSOR_FP16 = 1,  /* scales: 1 fp16 */
+  B2G_SCALE_CHANNEL_FP16 = 2, /* scales: [N] fp16 */
+  B2G_SCALE_CHANNEL_FP32 = 3  /* scales: [N] fp32 */
+};
+
+enum { B2G_LAYOUT_KN = 0, B2G_LAYOUT_NK = 1 };
+
+/* Fusion flags (bit mask).  None of these exist in the reference, which runs
+ * one GEMV per launch; they implement the decode-MLP dataflow of its ONNX
+ * graph (kernels/opt_loop/fp8_accuracy/capture_real_activations.py:39-42). */
+enum {
+  B2G_FUSE_NONE = 0,
+  B2G_FUSE_GATE_UP_SILU = 1, /* two weight planes (gate, up) of width N;
+                                y = fp16(SiLU(fp16(g)) * fp16(u)) */
+  B2G_FUSE_RMSNORM_INPUT = 2, /* x rows are RMS-normalised (gamma = 1) first */
+  B2G_FUSE_RESIDUAL_ADD = 4   /* y = fp16(residual + fp16(x W s)) */
+};
+
+/* Plugin-creator fields (the planned IPluginV3 creator's PluginFields:
+ * in_features / out_features / weight dtype / scale mode,
+ * tensorrt_custom_tactic_kernel_b07f17a4.plan.md:57-58, plus what the
+ * library adds: layout, max rows, fusion and the tensor-parallel slot). */
+typedef struct {
+  int32_t in_features;   /* K */
+  int32_t out_features;  /* N (per weight plane) */
+  int32_t weight_dtype;  /* B2G_DTYPE_* */
+  int32_t scale_mode;    /* B2G_SCALE_* */
+  int32_t weight_layout; /* B2G_LAYOUT_* of the unpacked weights given to prepack */
+  int32_t max_m;         /* 1..8 rows (decode tokens) per call */
+  int32_t fuse;          /* B2G_FUSE_* mask */
+  int32_t tp_rank;       /* informational: this shard's rank */
+  int32_t tp_size;       /* informational: number of shards (1 = unsharded) */
+} b2g_fields;
+
+typedef struct b2g_op b2g_op;
+
+/* Per-call arguments of b2g_enqueue_ex. */
+typedef struct {
+  int32_t m;              /* rows of x, 1..max_m */
+  const void* x;          /* [m, ldx] fp16 */
+  int64_t ldx;
+  const void* packed_w;   /* from b2g_prepack */
+  const void* scales;     /* per scale_mode; GATE_UP_SILU: gate then up
+                             ([2][N] per-channel, or 2 tensor scalars) */
+  const void* residual;   /* [m, ldr] fp16, FUSE_RESIDUAL_ADD only (may alias y) */
+  int64_t ldr;
+  void* y;                /* [m, ldy] fp16 */
+  int64_t ldy;
+  void* workspace;        /* b2g_workspace_size bytes, zeroed once by b2g_workspace_init */
+  float rms_eps;          /* FUSE_RMSNORM_INPUT epsilon (Llama: 1e-5) */
+  int32_t pdl;            /* 1: launch with programmatic dependent launch */
+} b2g_enqueue_args;
+
+/* Status string. */
+const char* b2g_status_string(b2g_status s);
+
+/* Library version (major*10000 + minor*100 + patch). */
+int32_t b2g_version(void);
+
+/* Plugin creator: validates the fields and plans the launch for the current
+ * device.  Replaces the reference's compile-time Tiling/variant tables
+ * (kernels/gemv_fp8.cu:192-234), which only accept N in {8192, 3072}. */
+b2g_status b2g_create(const b2g_fields* fields, b2g_op** out);
+b2g_status b2g_destroy(b2g_op* op);
+
+/* Tuning options (the reference's CLI knobs variant/grid/KU,
+ * kernels/gemv_fp8.cu:820-901, become per-op options).
+ *  B2G_OPT_MATH:       0 = tensor-core m16n8k16 tiles (default),
+ *                      1 = CUDA-core FFMA with the same data layout.
+ *  B2G_OPT_GRID:       CTA count, 0 = one per SM (default).
+ *  B2G_OPT_MAX_STAGES: cap on the shared-memory pipeline depth (2..16). */
+enum { B2G_OPT_MATH = 1, B2G_OPT_GRID = 2, B2G_OPT_MAX_STAGES = 3 };
+b2g_status b2g_op_set_option(b2g_op* op, int32_t key, int32_t value);
+
+/* The launch plan chosen for calls with m rows. */
+typedef struct {
+  int32_t grid;             /* CTAs (one per SM) */
+  int32_t ksplit;           /* K ranges */
+  int32_t kblocks_per_vtile;
+  int32_t n_tiles;          /* 16-channel output tiles */
+  int64_t total_units;      /* stream units (512 B per weight plane) */
+  int32_t unit_bytes;
+  int32_t n_stages;         /* TMA pipeline depth */
+  int32_t stage_bytes;
+  int64_t smem_bytes;       /* dynamic shared memory per CTA */
+  int32_t max_contrib;      /* max CTAs sharing one virtual tile */
+  int32_t n_slots;          /* virtual tiles per CTA (max) */
+  int32_t x_kblocks;        /* 32-wide k blocks of x staged per CTA */
+  int32_t math;
+} b2g_plan_info;
+b2g_status b2g_op_query(const b2g_op* op, int32_t m, b2g_plan_info* info);
+
+/* Bytes of the pre-packed weight buffer.  (The reference streams the raw
+ * [K, N] bytes, kernels/gemv_fp8.cu:93; the library streams a tile layout.) */
+b2g_status b2g_prepack_size(const b2g_op* op, size_t* bytes);
+
+/* Device-side repack of unpacked weights (op's dtype and layout, ld = row
+ * stride in elements of the unpacked matrix, 0 = dense) into the streaming
+ * tile layout.  GATE_UP_SILU takes the up plane in w_plane1, else NULL. */
+b2g_status b2g_prepack(const b2g_op* op, const void* w_plane0, const void* w_plane1,
+                       int64_t ld, void* packed, b2g_stream_t stream);
+
+/* Device-side E4M3 quantisation of fp16 weights [K, N] (KN) or [N, K] (NK)
+ * under a scale mode; writes E4M3 codes in the same layout and the scales.
+ * NONE is pack_e4m3 (kernels/gemv_fp8.cu:297-304); TENSOR_FP16/CHANNEL_FP16
+ * are check_real's scale + pre-divide (kernels/gemv_fp8.cu:515-543);
+ * CHANNEL_FP32 is s = max(amax,1e-12)/448 in fp32, q = e4m3(w / s). */
+b2g_status b2g_quantize_e4m3(const void* w16, int32_t K, int32_t N, int32_t layout,
+                             int32_t scale_mode, void* w8, void* scales, b2g_stream_t stream);
+
+/* Workspace bytes for calls with up to m rows, and its one-time zeroing
+ * (the kernels leave it zeroed after every complete call).  Replaces the
+ * reference's caller-provided y_acc that run_gemv memsets on every call
+ * (kernels/gemv_fp8.cu:276-283). */
+b2g_status b2g_workspace_size(const b2g_op* op, int32_t m, size_t* bytes);
+b2g_status b2g_workspace_init(const b2g_op* op, void* workspace, b2g_stream_t stream);
+
+/* enqueue(x, W, scales) -> y: the plugin's enqueue.  One kernel launch
+ * replaces the reference's run_gemv (memset + gemv_chunk_kernel + cast,
+ * kernels/gemv_fp8.cu:276-283; kernels/gemv_fp16.cu:262-271). */
+b2g_status b2g_enqueue(const b2g_op* op, int32_t m, const void* x, const void* packed_w,
+                       const void* scales, void* y, void* workspace, b2g_stream_t stream);
+b2g_status b2g_enqueue_ex(const b2g_op* op, const b2g_enqueue_args* args, b2g_stream_t stream);
+
+/* Reads (and optionally clears) the device error word that kernels set when
+ * a bounded wait expires.  Synchronises the current device. */
+b2g_status b2g_device_error(int32_t* code, int32_t clear);
+
+/* ------------------------------------------------------------------------
+ * Decode MLP stack: n_layers x [RMSNorm -> fused gate||up + SiLU*up -> down +
+ * residual], hidden state updated in place.  No reference counterpart (the
+ * reference runs single GEMVs); the layer dataflow is its ONNX graph's
+ * (capture_real_activations.py:39-42).
+ * ------------------------------------------------------------------------ */
+typedef struct {
+  int32_t hidden;        /* 3072 */
+  int32_t intermediate;  /* 8192 (per tensor-parallel shard: 8192 / tp_size) */
+  int32_t n_layers;      /* 28 */
+  int32_t weight_dtype;
+  int32_t scale_mode;
+  int32_t max_m;
+  float rms_eps;
+  int32_t tp_rank;
+  int32_t tp_size;
+} b2g_stack_fields;
+
+typedef struct b2g_stack b2g_stack;
+
+b2g_status b2g_stack_create(const b2g_stack_fields* fields, b2g_stack** out);
+b2g_status b2g_stack_destroy(b2g_stack* st);
+/* The fused gate||up op and the down op the stack uses (owned by the stack),
+ * for prepacking layer weights. */
+b2g_status b2g_stack_ops(const b2g_stack* st, const b2g_op** gate_up, const b2g_op** down);
+b2g_status b2g_stack_set_layer(b2g_stack* st, int32_t layer, const void* packed_gate_up,
+                               const void* scales_gate_up, const void* packed_down,
+                               const void* scales_down);
+b2g_status b2g_stack_workspace_size(const b2g_stack* st, int32_t m, size_t* bytes);
+b2g_status b2g_stack_workspace_init(const b2g_stack* st, void* workspace, b2g_stream_t stream);
+/* h [m, hidden] fp16 is read and overwritten; act is [m, intermediate] fp16
+ * scratch.  Launches 2 kernels per layer chained with programmatic dependent
+ * launch.  tp_size > 1 is not handled here (see the Python TP driver). */
+b2g_status b2g_stack_enqueue(const b2g_stack* st, int32_t m, void* h, void* act,
+                             void* workspace, b2g_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200GEMV_H_ */

@@ -1,0 +1,516 @@
+// api.cpp -- the C ABI (include/b200gemv.h): op planning, validation,
+// prepack/quantise, enqueue and the decode-MLP stack driver.
+//
+// Host-side replacement of the reference's launch plumbing
+// (kernels/gemv_fp8.cu:192-283, kernels/gemv_fp16.cu:198-271): instead of a
+// compile-time table of (threads, rows, vectors) variants for N in
+// {8192, 3072} and a tuned split count, the plan below derives the stream-K
+// partition, pipeline depth and shared-memory layout from the shape and the
+// device (SM count, shared memory per block).
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <vector>
+
+#include "../../include/b200gemv.h"
+#include "gemv.h"
+
+using namespace b2g;
+
+struct b2g_op {
+  b2g_fields f;
+  int planes, wbytes, kpb;
+  int K, N, Kp, n_tiles, kb_total, ksplit, kbpv;
+  long long total_units;
+  int unit_bytes;
+  size_t packed_bytes;
+  int device, num_sms, smem_optin;
+  int grid, grid_override;
+  int max_contrib, n_slots, xk_cap;
+  int math, max_stages;
+};
+
+struct b2g_stack {
+  b2g_stack_fields f;
+  b2g_op* gu;
+  b2g_op* dn;
+  struct Layer {
+    const void *pgu, *sgu, *pd, *sd;
+  };
+  std::vector<Layer> layers;
+};
+
+namespace {
+
+constexpr int kMaxM = 8;
+constexpr int kMaxStages = 16;
+constexpr int kStageUnits = kConsumerWarps * 2;
+
+b2g_status cuda_status(cudaError_t e) { return e == cudaSuccess ? B2G_OK : B2G_ERR_CUDA; }
+
+std::mutex g_mu;
+bool g_limit_set[64];
+int* g_err_word[64];
+
+b2g_status ensure_device_setup(int dev, int smem_optin) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (dev < 0 || dev >= 64) return B2G_ERR_UNSUPPORTED;
+  if (!g_limit_set[dev]) {
+    if (gemv_set_smem_limit(smem_optin) != cudaSuccess) return B2G_ERR_CUDA;
+    int* w = device_error_word();
+    if (!w) return B2G_ERR_CUDA;
+    g_err_word[dev] = w;
+    g_limit_set[dev] = true;
+  }
+  return B2G_OK;
+}
+
+long long cta_of(long long u, long long T, int G) { return ((u + 1) * G + T - 1) / T - 1; }
+
+// Stream-K partition statistics for a grid of G CTAs.
+void plan_partition(b2g_op* op) {
+  const long long T = op->total_units;
+  const int G = op->grid;
+  int max_slots = 0, max_kx = 0;
+  const int kx_per_ks = op->kbpv * op->kpb / 32;
+  for (int c = 0; c < G; ++c) {
+    const long long u0 = (long long)c * T / G, u1 = (long long)(c + 1) * T / G;
+    if (u1 <= u0) continue;
+    const long long vf = u0 / op->kbpv, vl = (u1 - 1) / op->kbpv;
+    max_slots = std::max(max_slots, (int)(vl - vf + 1));
+    const int ks_lo = (int)(vf / op->n_tiles), ks_hi = (int)(vl / op->n_tiles);
+    max_kx = std::max(max_kx, (ks_hi + 1 - ks_lo) * kx_per_ks);
+  }
+  int max_contrib = 1;
+  const long long n_vt = (long long)op->ksplit * op->n_tiles;
+  for (long long vt = 0; vt < n_vt; ++vt) {
+    const long long a = vt * op->kbpv;
+    max_contrib = std::max(max_contrib, (int)(cta_of(a + op->kbpv - 1, T, G) - cta_of(a, T, G)) + 1);
+  }
+  op->n_slots = max_slots;
+  op->xk_cap = max_kx;
+  op->max_contrib = max_contrib;
+}
+
+struct LaunchPlan {
+  int n_stages, off_misc, off_ring, off_slots, off_x;
+  size_t smem;
+};
+
+bool plan_launch(const b2g_op* op, int m, LaunchPlan* lp) {
+  const int unit = op->unit_bytes;
+  const size_t stage_bytes = (size_t)kStageUnits * unit;
+  const int off_misc = 16 * kMaxStages;
+  const int misc = 4 * (op->n_slots + 1 + 8 + 8 * kConsumerWarps);
+  const int off_ring = (off_misc + misc + 127) / 128 * 128;
+  const size_t slots = (size_t)op->n_slots * kConsumerWarps * op->planes * kUnitPlaneBytes;
+  const size_t xbytes = (size_t)op->xk_cap * m * 64;
+  const size_t fixed = off_ring + slots + xbytes;
+  if (fixed >= (size_t)op->smem_optin) return false;
+  int ns = (int)(((size_t)op->smem_optin - fixed) / stage_bytes);
+  ns = std::min(ns, std::min(kMaxStages, op->max_stages));
+  if (ns < 2) return false;
+  lp->n_stages = ns;
+  lp->off_misc = off_misc;
+  lp->off_ring = off_ring;
+  lp->off_slots = (int)(off_ring + ns * stage_bytes);
+  lp->off_x = (int)(lp->off_slots + slots);
+  lp->smem = lp->off_x + xbytes;
+  return true;
+}
+
+b2g_status replan(b2g_op* op) {
+  op->grid = (int)std::min<long long>(op->total_units, op->grid_override > 0 ? op->grid_override : op->num_sms);
+  plan_partition(op);
+  LaunchPlan lp;
+  if (!plan_launch(op, op->f.max_m, &lp)) return B2G_ERR_OOM;
+  return B2G_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+const char* b2g_status_string(b2g_status s) {
+  switch (s) {
+    case B2G_OK: return "ok";
+    case B2G_ERR_INVALID: return "invalid argument";
+    case B2G_ERR_UNSUPPORTED: return "unsupported";
+    case B2G_ERR_CUDA: return "CUDA error";
+    case B2G_ERR_PEER_TIMEOUT: return "peer wait timed out";
+    case B2G_ERR_OOM: return "out of shared memory or workspace";
+    case B2G_ERR_DEVICE: return "device-side error";
+  }
+  return "unknown status";
+}
+
+int32_t b2g_version(void) { return 100; }
+
+b2g_status b2g_create(const b2g_fields* f, b2g_op** out) {
+  if (!f || !out) return B2G_ERR_INVALID;
+  *out = nullptr;
+  if (f->in_features <= 0 || f->out_features <= 0) return B2G_ERR_INVALID;
+  if (f->weight_dtype != B2G_DTYPE_FP16 && f->weight_dtype != B2G_DTYPE_FP8_E4M3) return B2G_ERR_INVALID;
+  if (f->scale_mode < B2G_SCALE_NONE || f->scale_mode > B2G_SCALE_CHANNEL_FP32) return B2G_ERR_INVALID;
+  if (f->weight_layout != B2G_LAYOUT_KN && f->weight_layout != B2G_LAYOUT_NK) return B2G_ERR_INVALID;
+  if (f->max_m < 1 || f->max_m > kMaxM) return B2G_ERR_UNSUPPORTED;
+  if (f->fuse & ~(B2G_FUSE_GATE_UP_SILU | B2G_FUSE_RMSNORM_INPUT | B2G_FUSE_RESIDUAL_ADD))
+    return B2G_ERR_INVALID;
+  if ((f->fuse & B2G_FUSE_GATE_UP_SILU) && (f->fuse & B2G_FUSE_RESIDUAL_ADD)) return B2G_ERR_UNSUPPORTED;
+  if (f->tp_size < 0 || (f->tp_size > 0 && (f->tp_rank < 0 || f->tp_rank >= f->tp_size)))
+    return B2G_ERR_INVALID;
+
+  b2g_op* op = new (std::nothrow) b2g_op();
+  if (!op) return B2G_ERR_OOM;
+  op->f = *f;
+  op->planes = (f->fuse & B2G_FUSE_GATE_UP_SILU) ? 2 : 1;
+  op->wbytes = f->weight_dtype == B2G_DTYPE_FP8_E4M3 ? 1 : 2;
+  op->kpb = op->wbytes == 1 ? 32 : 16;
+  op->K = f->in_features;
+  op->N = f->out_features;
+  op->Kp = (op->K + 31) / 32 * 32;
+  op->kb_total = op->Kp / op->kpb;
+  op->n_tiles = (op->N + kTileCh - 1) / kTileCh;
+  op->ksplit = 1;
+  for (int ks : {8, 4, 2}) {
+    if (op->K / ks >= 2048 && op->kb_total % ks == 0 && ((op->kb_total / ks) * op->kpb) % 32 == 0) {
+      op->ksplit = ks;
+      break;
+    }
+  }
+  op->kbpv = op->kb_total / op->ksplit;
+  op->total_units = (long long)op->n_tiles * op->kb_total;
+  op->unit_bytes = op->planes * kUnitPlaneBytes;
+  op->packed_bytes = (size_t)op->total_units * op->unit_bytes;
+  op->math = kMathMma;
+  op->max_stages = kMaxStages;
+
+  cudaError_t e = cudaGetDevice(&op->device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&op->num_sms, cudaDevAttrMultiProcessorCount, op->device);
+  if (e == cudaSuccess)
+    e = cudaDeviceGetAttribute(&op->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, op->device);
+  if (e != cudaSuccess) {
+    delete op;
+    return B2G_ERR_CUDA;
+  }
+  b2g_status st = replan(op);
+  if (st != B2G_OK) {
+    delete op;
+    return st;
+  }
+  *out = op;
+  return B2G_OK;
+}
+
+b2g_status b2g_destroy(b2g_op* op) {
+  delete op;
+  return B2G_OK;
+}
+
+b2g_status b2g_op_set_option(b2g_op* op, int32_t key, int32_t value) {
+  if (!op) return B2G_ERR_INVALID;
+  switch (key) {
+    case B2G_OPT_MATH:
+      if (value != kMathMma && value != kMathFfma) return B2G_ERR_INVALID;
+      op->math = value;
+      return B2G_OK;
+    case B2G_OPT_GRID:
+      if (value < 0) return B2G_ERR_INVALID;
+      op->grid_override = value;
+      return replan(op);
+    case B2G_OPT_MAX_STAGES:
+      if (value < 2 || value > kMaxStages) return B2G_ERR_INVALID;
+      op->max_stages = value;
+      return replan(op);
+  }
+  return B2G_ERR_INVALID;
+}
+
+b2g_status b2g_op_query(const b2g_op* op, int32_t m, b2g_plan_info* info) {
+  if (!op || !info || m < 1 || m > op->f.max_m) return B2G_ERR_INVALID;
+  LaunchPlan lp;
+  if (!plan_launch(op, m, &lp)) return B2G_ERR_OOM;
+  info->grid = op->grid;
+  info->ksplit = op->ksplit;
+  info->kblocks_per_vtile = op->kbpv;
+  info->n_tiles = op->n_tiles;
+  info->total_units = op->total_units;
+  info->unit_bytes = op->unit_bytes;
+  info->n_stages = lp.n_stages;
+  info->stage_bytes = kStageUnits * op->unit_bytes;
+  info->smem_bytes = (int64_t)lp.smem;
+  info->max_contrib = op->max_contrib;
+  info->n_slots = op->n_slots;
+  info->x_kblocks = op->xk_cap;
+  info->math = op->math;
+  return B2G_OK;
+}
+
+b2g_status b2g_prepack_size(const b2g_op* op, size_t* bytes) {
+  if (!op || !bytes) return B2G_ERR_INVALID;
+  *bytes = op->packed_bytes;
+  return B2G_OK;
+}
+
+b2g_status b2g_prepack(const b2g_op* op, const void* w0, const void* w1, int64_t ld, void* packed,
+                       b2g_stream_t stream) {
+  if (!op || !w0 || !packed) return B2G_ERR_INVALID;
+  if (op->planes == 2 && !w1) return B2G_ERR_INVALID;
+  if (op->planes == 1 && w1) return B2G_ERR_INVALID;
+  if (!aligned(packed, 16)) return B2G_ERR_INVALID;
+  const long long dense = op->f.weight_layout == B2G_LAYOUT_KN ? op->N : op->K;
+  if (ld == 0) ld = dense;
+  if (ld < dense) return B2G_ERR_INVALID;
+  const void* planes[2] = {w0, w1};
+  for (int pl = 0; pl < op->planes; ++pl) {
+    cudaError_t e = launch_prepack(planes[pl], ld, op->f.weight_layout, op->wbytes, op->K, op->N, pl,
+                                   op->planes, op->ksplit, op->kbpv, op->n_tiles, op->kb_total,
+                                   static_cast<uint8_t*>(packed), reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return B2G_ERR_CUDA;
+  }
+  return B2G_OK;
+}
+
+b2g_status b2g_quantize_e4m3(const void* w16, int32_t K, int32_t N, int32_t layout, int32_t scale_mode,
+                             void* w8, void* scales, b2g_stream_t stream) {
+  if (!w16 || !w8 || K <= 0 || N <= 0) return B2G_ERR_INVALID;
+  if (layout != B2G_LAYOUT_KN && layout != B2G_LAYOUT_NK) return B2G_ERR_INVALID;
+  if (scale_mode < B2G_SCALE_NONE || scale_mode > B2G_SCALE_CHANNEL_FP32) return B2G_ERR_INVALID;
+  if (scale_mode != B2G_SCALE_NONE && !scales) return B2G_ERR_INVALID;
+  return cuda_status(launch_quantize(static_cast<const __half*>(w16), K, N, layout, scale_mode,
+                                     static_cast<uint8_t*>(w8), scales,
+                                     reinterpret_cast<cudaStream_t>(stream)));
+}
+
+static size_t ws_partials_bytes(const b2g_op* op) {
+  return (size_t)op->ksplit * op->n_tiles * op->max_contrib * op->planes * kUnitPlaneBytes;
+}
+
+b2g_status b2g_workspace_size(const b2g_op* op, int32_t m, size_t* bytes) {
+  if (!op || !bytes || m < 1 || m > op->f.max_m) return B2G_ERR_INVALID;
+  *bytes = ws_partials_bytes(op) + (size_t)(op->n_tiles + 63) / 64 * 256;
+  return B2G_OK;
+}
+
+b2g_status b2g_workspace_init(const b2g_op* op, void* ws, b2g_stream_t stream) {
+  if (!op || !ws) return B2G_ERR_INVALID;
+  size_t bytes = 0;
+  b2g_workspace_size(op, op->f.max_m, &bytes);
+  return cuda_status(cudaMemsetAsync(ws, 0, bytes, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+b2g_status b2g_enqueue_ex(const b2g_op* op, const b2g_enqueue_args* a, b2g_stream_t stream) {
+  if (!op || !a) return B2G_ERR_INVALID;
+  if (a->m < 1 || a->m > op->f.max_m) return B2G_ERR_INVALID;
+  if (!a->x || !a->packed_w || !a->y || !a->workspace) return B2G_ERR_INVALID;
+  if (op->f.scale_mode != B2G_SCALE_NONE && !a->scales) return B2G_ERR_INVALID;
+  const bool resid = (op->f.fuse & B2G_FUSE_RESIDUAL_ADD) != 0;
+  if (resid && !a->residual) return B2G_ERR_INVALID;
+  if (a->ldx < op->K || a->ldy < op->N || (resid && a->ldr < op->N)) return B2G_ERR_INVALID;
+  if (!aligned(a->packed_w, 16) || !aligned(a->workspace, 16)) return B2G_ERR_INVALID;
+  if (!aligned(a->x, 2) || !aligned(a->y, 2)) return B2G_ERR_INVALID;
+  if (op->f.scale_mode == B2G_SCALE_CHANNEL_FP32 && !aligned(a->scales, 4)) return B2G_ERR_INVALID;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B2G_ERR_CUDA;
+  if (dev != op->device) return B2G_ERR_INVALID;
+  b2g_status st = ensure_device_setup(dev, op->smem_optin);
+  if (st != B2G_OK) return st;
+  LaunchPlan lp;
+  if (!plan_launch(op, a->m, &lp)) return B2G_ERR_OOM;
+
+  GemvParams p = {};
+  p.packed = static_cast<const uint8_t*>(a->packed_w);
+  p.x = static_cast<const __half*>(a->x);
+  p.ldx = a->ldx;
+  p.scales = a->scales;
+  p.residual = static_cast<const __half*>(a->residual);
+  p.ldr = a->ldr;
+  p.y = static_cast<__half*>(a->y);
+  p.ldy = a->ldy;
+  p.partials = static_cast<float*>(a->workspace);
+  p.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(a->workspace) + ws_partials_bytes(op));
+  p.error = g_err_word[dev];
+  p.total_units = op->total_units;
+  p.grid = op->grid;
+  p.n_tiles = op->n_tiles;
+  p.kb_total = op->kb_total;
+  p.ksplit = op->ksplit;
+  p.kbpv = op->kbpv;
+  p.M = a->m;
+  p.K = op->K;
+  p.N = op->N;
+  p.scale_mode = op->f.scale_mode;
+  p.rmsnorm = (op->f.fuse & B2G_FUSE_RMSNORM_INPUT) ? 1 : 0;
+  p.residual_add = resid ? 1 : 0;
+  p.rms_eps = a->rms_eps;
+  p.max_contrib = op->max_contrib;
+  p.n_slots = op->n_slots;
+  p.xk_cap = op->xk_cap;
+  p.stage_units = kStageUnits;
+  p.n_stages = lp.n_stages;
+  p.off_misc = lp.off_misc;
+  p.off_ring = lp.off_ring;
+  p.off_slots = lp.off_slots;
+  p.off_x = lp.off_x;
+  return cuda_status(launch_gemv(p, op->planes, op->wbytes, op->math, lp.smem, a->pdl != 0,
+                                 reinterpret_cast<cudaStream_t>(stream)));
+}
+
+b2g_status b2g_enqueue(const b2g_op* op, int32_t m, const void* x, const void* packed_w, const void* scales,
+                       void* y, void* workspace, b2g_stream_t stream) {
+  if (!op) return B2G_ERR_INVALID;
+  if (op->f.fuse & B2G_FUSE_RESIDUAL_ADD) return B2G_ERR_INVALID;  // needs b2g_enqueue_ex
+  b2g_enqueue_args a = {};
+  a.m = m;
+  a.x = x;
+  a.ldx = op->K;
+  a.packed_w = packed_w;
+  a.scales = scales;
+  a.y = y;
+  a.ldy = op->N;
+  a.workspace = workspace;
+  a.rms_eps = 1e-5f;
+  a.pdl = 0;
+  return b2g_enqueue_ex(op, &a, stream);
+}
+
+b2g_status b2g_device_error(int32_t* code, int32_t clear) {
+  if (!code) return B2G_ERR_INVALID;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B2G_ERR_CUDA;
+  int* w = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (dev >= 0 && dev < 64) w = g_err_word[dev];
+  }
+  if (!w) {
+    *code = 0;
+    return B2G_OK;
+  }
+  if (cudaDeviceSynchronize() != cudaSuccess) return B2G_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return B2G_ERR_CUDA;
+  *code = v;
+  if (clear && cudaMemset(w, 0, sizeof(int)) != cudaSuccess) return B2G_ERR_CUDA;
+  return B2G_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Stack
+// ---------------------------------------------------------------------------
+b2g_status b2g_stack_create(const b2g_stack_fields* f, b2g_stack** out) {
+  if (!f || !out) return B2G_ERR_INVALID;
+  *out = nullptr;
+  if (f->hidden <= 0 || f->intermediate <= 0 || f->n_layers <= 0) return B2G_ERR_INVALID;
+  if (f->tp_size > 1) return B2G_ERR_UNSUPPORTED;
+  b2g_fields g = {};
+  g.in_features = f->hidden;
+  g.out_features = f->intermediate;
+  g.weight_dtype = f->weight_dtype;
+  g.scale_mode = f->scale_mode;
+  g.weight_layout = B2G_LAYOUT_KN;
+  g.max_m = f->max_m;
+  g.fuse = B2G_FUSE_GATE_UP_SILU | B2G_FUSE_RMSNORM_INPUT;
+  g.tp_rank = f->tp_rank;
+  g.tp_size = f->tp_size;
+  b2g_fields d = g;
+  d.in_features = f->intermediate;
+  d.out_features = f->hidden;
+  d.fuse = B2G_FUSE_RESIDUAL_ADD;
+  auto* st = new (std::nothrow) b2g_stack();
+  if (!st) return B2G_ERR_OOM;
+  st->f = *f;
+  b2g_status s = b2g_create(&g, &st->gu);
+  if (s == B2G_OK) s = b2g_create(&d, &st->dn);
+  if (s != B2G_OK) {
+    b2g_destroy(st->gu);
+    b2g_destroy(st->dn);
+    delete st;
+    return s;
+  }
+  st->layers.assign(f->n_layers, b2g_stack::Layer{nullptr, nullptr, nullptr, nullptr});
+  *out = st;
+  return B2G_OK;
+}
+
+b2g_status b2g_stack_destroy(b2g_stack* st) {
+  if (!st) return B2G_OK;
+  b2g_destroy(st->gu);
+  b2g_destroy(st->dn);
+  delete st;
+  return B2G_OK;
+}
+
+b2g_status b2g_stack_ops(const b2g_stack* st, const b2g_op** gu, const b2g_op** dn) {
+  if (!st) return B2G_ERR_INVALID;
+  if (gu) *gu = st->gu;
+  if (dn) *dn = st->dn;
+  return B2G_OK;
+}
+
+b2g_status b2g_stack_set_layer(b2g_stack* st, int32_t l, const void* pgu, const void* sgu, const void* pd,
+                               const void* sd) {
+  if (!st || l < 0 || l >= st->f.n_layers || !pgu || !pd) return B2G_ERR_INVALID;
+  if (st->f.scale_mode != B2G_SCALE_NONE && (!sgu || !sd)) return B2G_ERR_INVALID;
+  st->layers[l] = b2g_stack::Layer{pgu, sgu, pd, sd};
+  return B2G_OK;
+}
+
+b2g_status b2g_stack_workspace_size(const b2g_stack* st, int32_t m, size_t* bytes) {
+  if (!st || !bytes) return B2G_ERR_INVALID;
+  size_t a = 0, b = 0;
+  b2g_status s = b2g_workspace_size(st->gu, m, &a);
+  if (s == B2G_OK) s = b2g_workspace_size(st->dn, m, &b);
+  *bytes = std::max(a, b);
+  return s;
+}
+
+b2g_status b2g_stack_workspace_init(const b2g_stack* st, void* ws, b2g_stream_t stream) {
+  if (!st || !ws) return B2G_ERR_INVALID;
+  size_t bytes = 0;
+  b2g_status s = b2g_stack_workspace_size(st, st->f.max_m, &bytes);
+  if (s != B2G_OK) return s;
+  return cuda_status(cudaMemsetAsync(ws, 0, bytes, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+b2g_status b2g_stack_enqueue(const b2g_stack* st, int32_t m, void* h, void* act, void* ws, b2g_stream_t stream) {
+  if (!st || !h || !act || !ws) return B2G_ERR_INVALID;
+  for (int l = 0; l < st->f.n_layers; ++l) {
+    const auto& L = st->layers[l];
+    if (!L.pgu || !L.pd) return B2G_ERR_INVALID;
+    b2g_enqueue_args a = {};
+    a.m = m;
+    a.x = h;
+    a.ldx = st->f.hidden;
+    a.packed_w = L.pgu;
+    a.scales = L.sgu;
+    a.y = act;
+    a.ldy = st->f.intermediate;
+    a.workspace = ws;
+    a.rms_eps = st->f.rms_eps;
+    a.pdl = 1;
+    b2g_status s = b2g_enqueue_ex(st->gu, &a, stream);
+    if (s != B2G_OK) return s;
+    b2g_enqueue_args d = {};
+    d.m = m;
+    d.x = act;
+    d.ldx = st->f.intermediate;
+    d.packed_w = L.pd;
+    d.scales = L.sd;
+    d.residual = h;
+    d.ldr = st->f.hidden;
+    d.y = h;
+    d.ldy = st->f.hidden;
+    d.workspace = ws;
+    d.pdl = 1;
+    s = b2g_enqueue_ex(st->dn, &d, stream);
+    if (s != B2G_OK) return s;
+  }
+  return B2G_OK;
+}
+
+}  // extern "C"

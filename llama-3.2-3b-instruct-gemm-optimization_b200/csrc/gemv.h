@@ -1,0 +1,72 @@
+// gemv.h -- internal interface between the host API (api.cpp) and the
+// kernels (gemv.cu, pack.cu).  Not part of the public C ABI.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace b2g {
+
+// Packed weight stream.
+//   A "unit" is what one warp consumes per step: 32 lanes x 16 B = 512 B per
+//   weight plane -- 16 output channels x 32 k (E4M3) or 16 x 16 k (FP16),
+//   arranged so each lane's 16 B are its m16n8k16 A-fragment registers.
+//   A "tile" is 16 output channels.  K is cut into `ksplit` equal k-ranges;
+//   a "virtual tile" (vt) is one tile over one k-range.  The stream is ordered
+//   [ks][tile][kb-in-range][plane][lane][16 B], so every CTA streams one
+//   contiguous byte range: units [u0, u1) with u0 = cta * T / grid.
+constexpr int kUnitPlaneBytes = 512;
+constexpr int kTileCh = 16;
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+
+enum MathKind : int { kMathMma = 0, kMathFfma = 1 };
+
+struct GemvParams {
+  const uint8_t* packed;
+  const __half* x;
+  long long ldx;
+  const void* scales;
+  const __half* residual;
+  long long ldr;
+  __half* y;
+  long long ldy;
+  float* partials;  // [n_vt][max_contrib][planes][32 lanes][4]
+  int* counters;    // [n_tiles]
+  int* error;
+  long long total_units;
+  int grid;
+  int n_tiles;
+  int kb_total;  // k-blocks (32 k for E4M3, 16 k for FP16) over padded K
+  int ksplit;
+  int kbpv;  // k-blocks per virtual tile
+  int M, K, N;
+  int scale_mode;
+  int rmsnorm;
+  int residual_add;
+  float rms_eps;
+  int max_contrib;
+  int n_slots;
+  int xk_cap;  // k32 blocks of x held in shared memory
+  int stage_units;
+  int n_stages;
+  int off_misc, off_ring, off_slots, off_x;  // shared-memory byte offsets
+};
+
+// Launch one GEMV (planes = 1 or 2, wbytes = 1 for E4M3 or 2 for FP16).
+cudaError_t launch_gemv(const GemvParams& p, int planes, int wbytes, int math, size_t smem,
+                        bool pdl, cudaStream_t stream);
+// Raises the dynamic shared-memory limit of every kernel variant.
+cudaError_t gemv_set_smem_limit(int bytes);
+
+// Pack / quantise kernels (pack.cu).
+cudaError_t launch_prepack(const void* w, long long ld, int layout, int wbytes, int K, int N,
+                           int plane, int planes, int ksplit, int kbpv, int n_tiles, int kb_total,
+                           uint8_t* packed, cudaStream_t stream);
+cudaError_t launch_quantize(const __half* w16, int K, int N, int layout, int scale_mode,
+                            uint8_t* w8, void* scales, cudaStream_t stream);
+
+int* device_error_word();  // address of the library's device error word (current device)
+
+}  // namespace b2g

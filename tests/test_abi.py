@@ -1,0 +1,87 @@
+"""The C-ABI library loads and exports what include/b200gemv.h declares (CPU).
+
+No kernel is launched here: argument validation happens before any CUDA
+call, so invalid requests are rejected identically with or without a GPU.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = ROOT / "include" / "b200gemv.h"
+
+
+def declared_functions():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(b2g_\w+)\s*\(", text)))
+
+
+def test_header_declarations_have_bindings(b2g):
+    decl = declared_functions()
+    assert len(decl) >= 20
+    assert sorted(b2g.SIGNATURES) == decl
+
+
+def test_library_exports_every_declared_symbol(b2g):
+    L = b2g.lib()
+    for name in declared_functions():
+        assert hasattr(L, name), name
+
+
+def test_status_strings_and_version(b2g):
+    L = b2g.lib()
+    assert L.b2g_version() >= 100
+    for s in range(7):
+        assert L.b2g_status_string(s)
+    assert L.b2g_status_string(0) == b"ok"
+
+
+@pytest.mark.parametrize("bad", [
+    dict(in_features=0), dict(out_features=-1), dict(weight_dtype=7), dict(scale_mode=9),
+    dict(weight_layout=3), dict(fuse=64), dict(tp_size=2, tp_rank=2),
+])
+def test_create_rejects_bad_fields(b2g, bad):
+    f = dict(in_features=3072, out_features=8192, weight_dtype=1, scale_mode=3, weight_layout=0,
+             max_m=8, fuse=0, tp_rank=0, tp_size=1)
+    f.update(bad)
+    h = ctypes.c_void_p()
+    st = b2g.lib().b2g_create(ctypes.byref(b2g.Fields(**f)), ctypes.byref(h))
+    assert st == b2g.ERR_INVALID and not h.value
+
+
+def test_create_rejects_unsupported(b2g):
+    h = ctypes.c_void_p()
+    f = b2g.Fields(3072, 8192, 1, 3, 0, 16, 0, 0, 1)  # max_m 16 > 8
+    assert b2g.lib().b2g_create(ctypes.byref(f), ctypes.byref(h)) == b2g.ERR_UNSUPPORTED
+    f = b2g.Fields(3072, 8192, 1, 3, 0, 8, b2g.FUSE_GATE_UP_SILU | b2g.FUSE_RESIDUAL_ADD, 0, 1)
+    assert b2g.lib().b2g_create(ctypes.byref(f), ctypes.byref(h)) == b2g.ERR_UNSUPPORTED
+
+
+def test_null_arguments_rejected(b2g):
+    L = b2g.lib()
+    assert L.b2g_create(None, None) == b2g.ERR_INVALID
+    n = ctypes.c_size_t()
+    assert L.b2g_prepack_size(None, ctypes.byref(n)) == b2g.ERR_INVALID
+    assert L.b2g_enqueue_ex(None, None, None) == b2g.ERR_INVALID
+    assert L.b2g_quantize_e4m3(None, 4, 4, 0, 0, None, None, None) == b2g.ERR_INVALID
+    assert L.b2g_stack_create(None, None) == b2g.ERR_INVALID
+    assert L.b2g_destroy(None) == b2g.OK
+
+
+def test_product_raises_without_library(b2g, monkeypatch, tmp_path):
+    """No silent fallback: a missing library is an error, not a CPU path."""
+    monkeypatch.setattr(b2g, "LIB_PATH", tmp_path / "missing.so")
+    monkeypatch.setattr(b2g, "_lib", None)
+    with pytest.raises(RuntimeError, match="missing"):
+        b2g.lib()
+
+
+def test_package_does_not_reference_the_oracle():
+    pkg = ROOT / "llama-3.2-3b-instruct-gemm-optimization_b200"
+    for p in list(pkg.rglob("*.py")) + list(pkg.rglob("*.cu")) + list(pkg.rglob("*.cpp")) + \
+            list(pkg.rglob("*.cuh")) + list(pkg.rglob("*.h")):
+        assert "oracle" not in p.read_text().lower(), p
