@@ -226,12 +226,12 @@ def run_ours(args):
     ws.zero_()
 
     def step():
-        for L in layers:
-            gu_op.enqueue(h, L["pgu"], L["sgu"], y=act, workspace=ws, pdl=True)
-            if rank == 0:
-                dn_op.enqueue(act, L["pd"], L["sd"], y=h, residual=h, workspace=ws, pdl=True)
-            else:
-                dn_op.enqueue(act, L["pd"], L["sd"], y=h, workspace=ws, pdl=True)
+        for i, L in enumerate(layers):
+            nxt = layers[(i + 1) % LAYERS]
+            gu_op.enqueue(h, L["pgu"], L["sgu"], y=act, workspace=ws, pdl=True,
+                          prefetch=(dn_op, L["pd"]))
+            dn_op.enqueue(act, L["pd"], L["sd"], y=h, residual=h if rank == 0 else None,
+                          workspace=ws, pdl=True, prefetch=(gu_op, nxt["pgu"]))
             if tp > 1:
                 dist.all_reduce(h)
 
@@ -288,8 +288,9 @@ def run_ours(args):
 
     # ---- dominant kernel: fused RMSNorm + gate||up + SiLU*up, 28 layers back to back
     def gu_sweep():
-        for L in layers:
-            gu_op.enqueue(h, L["pgu"], L["sgu"], y=act, workspace=ws, pdl=True)
+        for i, L in enumerate(layers):
+            gu_op.enqueue(h, L["pgu"], L["sgu"], y=act, workspace=ws, pdl=True,
+                          prefetch=(gu_op, layers[(i + 1) % LAYERS]["pgu"]))
     for _ in range(3):
         gu_sweep()
     reps = max(5, args.steps // 20)
@@ -309,9 +310,9 @@ def run_ours(args):
     ms_dn = None
 
     def dn_sweep():
-        for L in layers:
+        for i, L in enumerate(layers):
             dn_op.enqueue(act, L["pd"], L["sd"], y=h, residual=h if rank == 0 else None,
-                          workspace=ws, pdl=True)
+                          workspace=ws, pdl=True, prefetch=(dn_op, layers[(i + 1) % LAYERS]["pd"]))
     for _ in range(3):
         dn_sweep()
     ms_dn = timed(dn_sweep, reps) / (reps * LAYERS)

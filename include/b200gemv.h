@@ -103,7 +103,17 @@ typedef struct {
   int64_t ldy;
   void* workspace;        /* b2g_workspace_size bytes, zeroed once by b2g_workspace_init */
   float rms_eps;          /* FUSE_RMSNORM_INPUT epsilon (Llama: 1e-5) */
-  int32_t pdl;            /* 1: launch with programmatic dependent launch */
+  int32_t pdl;            /* 1: programmatic dependent launch.  The kernel then
+                             starts streaming packed_w before the preceding
+                             kernel in the stream has finished, so that kernel
+                             must not write packed_w (x, residual, scales,
+                             y and workspace are safe: they are touched only
+                             after the wait). */
+  const void* prefetch_packed; /* optional: packed weights of the kernel that
+                                  will follow this one in the stream; once its
+                                  own stream is issued, each CTA warms L2 with
+                                  the start of that kernel's range (NULL = off) */
+  const struct b2g_op* prefetch_op; /* the op prefetch_packed belongs to */
 } b2g_enqueue_args;
 
 /* Status string. */
@@ -120,11 +130,10 @@ b2g_status b2g_destroy(b2g_op* op);
 
 /* Tuning options (the reference's CLI knobs variant/grid/KU,
  * kernels/gemv_fp8.cu:820-901, become per-op options).
- *  B2G_OPT_MATH:       0 = tensor-core m16n8k16 tiles (default),
- *                      1 = CUDA-core FFMA with the same data layout.
- *  B2G_OPT_GRID:       CTA count, 0 = one per SM (default).
- *  B2G_OPT_MAX_STAGES: cap on the shared-memory pipeline depth (2..16). */
-enum { B2G_OPT_MATH = 1, B2G_OPT_GRID = 2, B2G_OPT_MAX_STAGES = 3 };
+ *  B2G_OPT_MATH: 0 = tensor-core m16n8k16 tiles (default),
+ *                1 = CUDA-core FFMA with the same data layout.
+ *  B2G_OPT_GRID: CTA count, 0 = one per SM (default). */
+enum { B2G_OPT_MATH = 1, B2G_OPT_GRID = 2 };
 b2g_status b2g_op_set_option(b2g_op* op, int32_t key, int32_t value);
 
 /* The launch plan chosen for calls with m rows. */
@@ -135,8 +144,7 @@ typedef struct {
   int32_t n_tiles;          /* 16-channel output tiles */
   int64_t total_units;      /* stream units (512 B per weight plane) */
   int32_t unit_bytes;
-  int32_t n_stages;         /* TMA pipeline depth */
-  int32_t stage_bytes;
+  int64_t inflight_bytes_per_cta; /* weight bytes each CTA keeps in flight */
   int64_t smem_bytes;       /* dynamic shared memory per CTA */
   int32_t max_contrib;      /* max CTAs sharing one virtual tile */
   int32_t n_slots;          /* virtual tiles per CTA (max) */

@@ -24,7 +24,7 @@ DTYPE = {"fp16": 0, "fp8_e4m3": 1}
 SCALE = {"none": 0, "tensor_fp16": 1, "channel_fp16": 2, "channel_fp32": 3}
 LAYOUT = {"KN": 0, "NK": 1}
 FUSE_NONE, FUSE_GATE_UP_SILU, FUSE_RMSNORM_INPUT, FUSE_RESIDUAL_ADD = 0, 1, 2, 4
-OPT_MATH, OPT_GRID, OPT_MAX_STAGES = 1, 2, 3
+OPT_MATH, OPT_GRID = 1, 2
 MATH_MMA, MATH_FFMA = 0, 1
 
 
@@ -45,15 +45,15 @@ class EnqueueArgs(ctypes.Structure):
                 ("packed_w", ctypes.c_void_p), ("scales", ctypes.c_void_p),
                 ("residual", ctypes.c_void_p), ("ldr", ctypes.c_int64), ("y", ctypes.c_void_p),
                 ("ldy", ctypes.c_int64), ("workspace", ctypes.c_void_p), ("rms_eps", ctypes.c_float),
-                ("pdl", ctypes.c_int32)]
+                ("pdl", ctypes.c_int32), ("prefetch_packed", ctypes.c_void_p),
+                ("prefetch_op", ctypes.c_void_p)]
 
 
 class PlanInfo(ctypes.Structure):
     _fields_ = [("grid", ctypes.c_int32), ("ksplit", ctypes.c_int32),
                 ("kblocks_per_vtile", ctypes.c_int32), ("n_tiles", ctypes.c_int32),
                 ("total_units", ctypes.c_int64), ("unit_bytes", ctypes.c_int32),
-                ("n_stages", ctypes.c_int32), ("stage_bytes", ctypes.c_int32),
-                ("smem_bytes", ctypes.c_int64), ("max_contrib", ctypes.c_int32),
+                ("inflight_bytes_per_cta", ctypes.c_int64), ("smem_bytes", ctypes.c_int64), ("max_contrib", ctypes.c_int32),
                 ("n_slots", ctypes.c_int32), ("x_kblocks", ctypes.c_int32), ("math", ctypes.c_int32)]
 
     def as_dict(self):
@@ -127,6 +127,11 @@ def _stream(stream):
     return ctypes.c_void_p(s.cuda_stream)
 
 
+def _rows_stride(t):
+    """Row stride in elements (a size-1 leading axis may carry any stride)."""
+    return t.stride(0) if t.shape[0] > 1 else t.shape[1]
+
+
 def _code(table, v):
     return table[v] if isinstance(v, str) else int(v)
 
@@ -196,18 +201,24 @@ class GemvOp:
 
     # -- enqueue --------------------------------------------------------
     def enqueue(self, x, packed, scales=None, y=None, workspace=None, residual=None,
-                rms_eps: float = 1e-5, pdl: bool = False, stream=None):
+                rms_eps: float = 1e-5, pdl: bool = False, stream=None, prefetch=None):
+        """y = op(x, W, scales).  prefetch=(next_op, next_packed) warms L2 with the
+        start of the weights the next launch in the stream will read."""
         import torch
         m = x.shape[0]
         if y is None:
             y = torch.empty((m, self.N), dtype=torch.float16, device=x.device)
         if workspace is None:
             workspace = self.workspace(x.device, stream)
-        a = EnqueueArgs(m, x.data_ptr(), x.stride(0), packed.data_ptr(),
+        if x.stride(-1) != 1 or y.stride(-1) != 1 or (residual is not None and residual.stride(-1) != 1):
+            raise ValueError("x, y and residual rows must be contiguous")
+        a = EnqueueArgs(m, x.data_ptr(), _rows_stride(x), packed.data_ptr(),
                         0 if scales is None else scales.data_ptr(),
                         0 if residual is None else residual.data_ptr(),
-                        0 if residual is None else residual.stride(0), y.data_ptr(), y.stride(0),
-                        workspace.data_ptr(), rms_eps, 1 if pdl else 0)
+                        0 if residual is None else _rows_stride(residual), y.data_ptr(),
+                        _rows_stride(y), workspace.data_ptr(), rms_eps, 1 if pdl else 0,
+                        None if prefetch is None else prefetch[1].data_ptr(),
+                        None if prefetch is None else prefetch[0].h)
         check(lib().b2g_enqueue_ex(self.h, ctypes.byref(a), _stream(stream)), "b2g_enqueue_ex")
         return y
 

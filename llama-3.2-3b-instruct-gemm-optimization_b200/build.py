@@ -34,16 +34,17 @@ def stale() -> bool:
     return any(d.stat().st_mtime > t for d in deps if d.exists())
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and not stale():
+def build(force: bool = False, verbose: bool = False, out: Path = LIB, defines=()) -> Path:
+    if not force and out == LIB and not stale():
         return LIB
     cmd = [nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC,-O2", "-shared",
-           "-I", str(HERE.parent / "include"), "-o", str(LIB)] + [str(CSRC / s) for s in SOURCES]
+           "-I", str(HERE.parent / "include"), *[f"-D{d}" for d in defines], "-o", str(out)] + \
+        [str(CSRC / s) for s in SOURCES]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)
-    return LIB
+    return out
 
 
 if __name__ == "__main__":

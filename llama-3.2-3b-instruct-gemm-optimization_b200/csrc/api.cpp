@@ -26,10 +26,10 @@ struct b2g_op {
   long long total_units;
   int unit_bytes;
   size_t packed_bytes;
-  int device, num_sms, smem_optin;
+  int device, num_sms, smem_optin, smem_per_sm;
   int grid, grid_override;
   int max_contrib, n_slots, xk_cap;
-  int math, max_stages;
+  int math;
 };
 
 struct b2g_stack {
@@ -45,8 +45,6 @@ struct b2g_stack {
 namespace {
 
 constexpr int kMaxM = 8;
-constexpr int kMaxStages = 16;
-constexpr int kStageUnits = kConsumerWarps * 2;
 
 b2g_status cuda_status(cudaError_t e) { return e == cudaSuccess ? B2G_OK : B2G_ERR_CUDA; }
 
@@ -95,35 +93,29 @@ void plan_partition(b2g_op* op) {
 }
 
 struct LaunchPlan {
-  int n_stages, off_misc, off_ring, off_slots, off_x;
+  int off_x, x_rs;
   size_t smem;
 };
 
+// Shared memory per CTA (one CTA per SM): flags, the per-warp partial slots,
+// and the M staged activation rows.
 bool plan_launch(const b2g_op* op, int m, LaunchPlan* lp) {
-  const int unit = op->unit_bytes;
-  const size_t stage_bytes = (size_t)kStageUnits * unit;
-  const int off_misc = 16 * kMaxStages;
-  const int misc = 4 * (op->n_slots + 1 + 8 + 8 * kConsumerWarps);
-  const int off_ring = (off_misc + misc + 127) / 128 * 128;
-  const size_t slots = (size_t)op->n_slots * kConsumerWarps * op->planes * kUnitPlaneBytes;
-  const size_t xbytes = (size_t)op->xk_cap * m * 64;
-  const size_t fixed = off_ring + slots + xbytes;
-  if (fixed >= (size_t)op->smem_optin) return false;
-  int ns = (int)(((size_t)op->smem_optin - fixed) / stage_bytes);
-  ns = std::min(ns, std::min(kMaxStages, op->max_stages));
-  if (ns < 2) return false;
-  lp->n_stages = ns;
-  lp->off_misc = off_misc;
-  lp->off_ring = off_ring;
-  lp->off_slots = (int)(off_ring + ns * stage_bytes);
-  lp->off_x = (int)(lp->off_slots + slots);
+  // Row stride = 32 (E4M3) or 16 (FP16) halves mod 64, so the eight rows of a
+  // B fragment load fall in distinct banks.
+  const int krange = op->xk_cap * 32;
+  const int x_rs = (krange + 63) / 64 * 64 + (op->wbytes == 1 ? 32 : 16);
+  const size_t xbytes = ((size_t)m * x_rs * 2 + 127) / 128 * 128;
+  const size_t slot_bytes = (size_t)op->n_slots * kWarps * op->planes * kUnitPlaneBytes;
+  lp->off_x = (int)(kOffSlots + slot_bytes);
+  lp->x_rs = x_rs;
   lp->smem = lp->off_x + xbytes;
-  return true;
+  return lp->smem <= (size_t)op->smem_optin;
 }
 
 b2g_status replan(b2g_op* op) {
   op->grid = (int)std::min<long long>(op->total_units, op->grid_override > 0 ? op->grid_override : op->num_sms);
   plan_partition(op);
+  if (op->n_slots > kMaxSlots) return B2G_ERR_UNSUPPORTED;
   LaunchPlan lp;
   if (!plan_launch(op, op->f.max_m, &lp)) return B2G_ERR_OOM;
   return B2G_OK;
@@ -176,7 +168,17 @@ b2g_status b2g_create(const b2g_fields* f, b2g_op** out) {
   op->kb_total = op->Kp / op->kpb;
   op->n_tiles = (op->N + kTileCh - 1) / kTileCh;
   op->ksplit = 1;
+  if (op->n_tiles > kMaxTiles) {
+    delete op;
+    return B2G_ERR_UNSUPPORTED;
+  }
+  if ((f->fuse & B2G_FUSE_RMSNORM_INPUT) && (op->K % 8) != 0) {
+    delete op;
+    return B2G_ERR_UNSUPPORTED;
+  }
+  // RMSNorm needs whole rows in one CTA: no K split.
   for (int ks : {8, 4, 2}) {
+    if (f->fuse & B2G_FUSE_RMSNORM_INPUT) break;
     if (op->K / ks >= 2048 && op->kb_total % ks == 0 && ((op->kb_total / ks) * op->kpb) % 32 == 0) {
       op->ksplit = ks;
       break;
@@ -184,15 +186,20 @@ b2g_status b2g_create(const b2g_fields* f, b2g_op** out) {
   }
   op->kbpv = op->kb_total / op->ksplit;
   op->total_units = (long long)op->n_tiles * op->kb_total;
+  if (op->total_units >= (1LL << 30)) {
+    delete op;
+    return B2G_ERR_UNSUPPORTED;
+  }
   op->unit_bytes = op->planes * kUnitPlaneBytes;
   op->packed_bytes = (size_t)op->total_units * op->unit_bytes;
   op->math = kMathMma;
-  op->max_stages = kMaxStages;
 
   cudaError_t e = cudaGetDevice(&op->device);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&op->num_sms, cudaDevAttrMultiProcessorCount, op->device);
   if (e == cudaSuccess)
     e = cudaDeviceGetAttribute(&op->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, op->device);
+  if (e == cudaSuccess)
+    e = cudaDeviceGetAttribute(&op->smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, op->device);
   if (e != cudaSuccess) {
     delete op;
     return B2G_ERR_CUDA;
@@ -217,14 +224,10 @@ b2g_status b2g_op_set_option(b2g_op* op, int32_t key, int32_t value) {
     case B2G_OPT_MATH:
       if (value != kMathMma && value != kMathFfma) return B2G_ERR_INVALID;
       op->math = value;
-      return B2G_OK;
+      return replan(op);
     case B2G_OPT_GRID:
       if (value < 0) return B2G_ERR_INVALID;
       op->grid_override = value;
-      return replan(op);
-    case B2G_OPT_MAX_STAGES:
-      if (value < 2 || value > kMaxStages) return B2G_ERR_INVALID;
-      op->max_stages = value;
       return replan(op);
   }
   return B2G_ERR_INVALID;
@@ -240,8 +243,7 @@ b2g_status b2g_op_query(const b2g_op* op, int32_t m, b2g_plan_info* info) {
   info->n_tiles = op->n_tiles;
   info->total_units = op->total_units;
   info->unit_bytes = op->unit_bytes;
-  info->n_stages = lp.n_stages;
-  info->stage_bytes = kStageUnits * op->unit_bytes;
+  info->inflight_bytes_per_cta = (int64_t)kThreads * 16 * (op->planes == 1 ? 16 : 16);
   info->smem_bytes = (int64_t)lp.smem;
   info->max_contrib = op->max_contrib;
   info->n_slots = op->n_slots;
@@ -292,7 +294,7 @@ static size_t ws_partials_bytes(const b2g_op* op) {
 
 b2g_status b2g_workspace_size(const b2g_op* op, int32_t m, size_t* bytes) {
   if (!op || !bytes || m < 1 || m > op->f.max_m) return B2G_ERR_INVALID;
-  *bytes = ws_partials_bytes(op) + (size_t)(op->n_tiles + 63) / 64 * 256;
+  *bytes = kCounterRegionBytes + ws_partials_bytes(op);
   return B2G_OK;
 }
 
@@ -331,8 +333,8 @@ b2g_status b2g_enqueue_ex(const b2g_op* op, const b2g_enqueue_args* a, b2g_strea
   p.ldr = a->ldr;
   p.y = static_cast<__half*>(a->y);
   p.ldy = a->ldy;
-  p.partials = static_cast<float*>(a->workspace);
-  p.counters = reinterpret_cast<int*>(static_cast<uint8_t*>(a->workspace) + ws_partials_bytes(op));
+  p.counters = static_cast<int*>(a->workspace);
+  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(a->workspace) + kCounterRegionBytes);
   p.error = g_err_word[dev];
   p.total_units = op->total_units;
   p.grid = op->grid;
@@ -349,13 +351,18 @@ b2g_status b2g_enqueue_ex(const b2g_op* op, const b2g_enqueue_args* a, b2g_strea
   p.rms_eps = a->rms_eps;
   p.max_contrib = op->max_contrib;
   p.n_slots = op->n_slots;
-  p.xk_cap = op->xk_cap;
-  p.stage_units = kStageUnits;
-  p.n_stages = lp.n_stages;
-  p.off_misc = lp.off_misc;
-  p.off_ring = lp.off_ring;
-  p.off_slots = lp.off_slots;
   p.off_x = lp.off_x;
+  p.x_rs = lp.x_rs;
+  p.x_tma = (aligned(a->x, 16) && (a->ldx % 8) == 0 && (op->K % 32) == 0) ? 1 : 0;
+  if (a->prefetch_op && a->prefetch_packed) {
+    const b2g_op* nx = a->prefetch_op;
+    if (!aligned(a->prefetch_packed, 16)) return B2G_ERR_INVALID;
+    p.pf_packed = static_cast<const uint8_t*>(a->prefetch_packed);
+    p.pf_total_units = nx->total_units;
+    p.pf_unit_bytes = nx->unit_bytes;
+    p.pf_grid = nx->grid;
+    p.pf_bytes = 131072;  // one CTA's initial loads (128 KB in flight per SM)
+  }
   return cuda_status(launch_gemv(p, op->planes, op->wbytes, op->math, lp.smem, a->pdl != 0,
                                  reinterpret_cast<cudaStream_t>(stream)));
 }
@@ -482,6 +489,7 @@ b2g_status b2g_stack_enqueue(const b2g_stack* st, int32_t m, void* h, void* act,
   for (int l = 0; l < st->f.n_layers; ++l) {
     const auto& L = st->layers[l];
     if (!L.pgu || !L.pd) return B2G_ERR_INVALID;
+    const auto& Ln = st->layers[(l + 1) % st->f.n_layers];
     b2g_enqueue_args a = {};
     a.m = m;
     a.x = h;
@@ -493,6 +501,8 @@ b2g_status b2g_stack_enqueue(const b2g_stack* st, int32_t m, void* h, void* act,
     a.workspace = ws;
     a.rms_eps = st->f.rms_eps;
     a.pdl = 1;
+    a.prefetch_packed = L.pd;
+    a.prefetch_op = st->dn;
     b2g_status s = b2g_enqueue_ex(st->gu, &a, stream);
     if (s != B2G_OK) return s;
     b2g_enqueue_args d = {};
@@ -507,6 +517,8 @@ b2g_status b2g_stack_enqueue(const b2g_stack* st, int32_t m, void* h, void* act,
     d.ldy = st->f.hidden;
     d.workspace = ws;
     d.pdl = 1;
+    d.prefetch_packed = Ln.pgu;
+    d.prefetch_op = st->gu;
     s = b2g_enqueue_ex(st->dn, &d, stream);
     if (s != B2G_OK) return s;
   }

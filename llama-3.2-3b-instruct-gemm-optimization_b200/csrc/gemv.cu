@@ -4,31 +4,31 @@
 //
 // This computes what the reference's run_gemv computes
 // (kernels/gemv_fp8.cu:276-283 -> gemv_chunk_kernel :91-151 -> cast :153-173;
-// kernels/gemv_fp16.cu:134-156), but is organised for B200:
+// kernels/gemv_fp16.cu:134-156), organised for B200:
 //
-//  * One CTA per SM.  The packed weight stream (gemv.h) is cut into `grid`
-//    equal contiguous byte ranges (stream-K), so every SM streams the same
-//    number of bytes whatever the shape -- no wave quantisation, no tail.
-//  * A producer warp streams the CTA's range into a shared-memory ring with
-//    1-D bulk TMA copies (cp.async.bulk, L2 evict-first), several stages in
-//    flight; it never waits on the previous kernel (weights are constant), so
-//    under programmatic dependent launch the stream starts while the previous
-//    kernel drains.
-//  * Eight consumer warps take units round-robin.  A unit is 16 output
-//    channels x 32 k (E4M3) or 16 k (FP16); each lane's 16 B are exactly its
-//    m16n8k16 A-fragment, so E4M3 is widened with cvt.rn.f16x2.e4m3x2 in
-//    registers and fed to mma.sync with x^T (k x 8 tokens) as the B operand:
-//    the M <= 8 decode rows fill the n = 8 side of the tile.  A CUDA-core
+//  * One CTA of 16 warps per SM.  The packed weight stream (gemv.h) is cut
+//    into `grid` equal contiguous ranges (stream-K), so every SM streams the
+//    same number of bytes whatever the shape: no wave quantisation, no tail.
+//  * Weights go straight from HBM into registers: each lane's 16 B of a unit
+//    (16 output channels x 32 k for E4M3, x 16 k for FP16) is exactly its
+//    m16n8k16 A fragment, loaded with ld.global.nc.L1::no_allocate (L2
+//    evict-first) 8-16 units ahead, 128 KB in flight per SM.  The first loads
+//    are issued before waiting on the previous kernel (weights are
+//    constant), and the tail of the stream warms L2 for the next kernel.
+//  * The M <= 8 activation rows are staged once per CTA in shared memory by
+//    bulk copy (RMSNorm applied there when fused), with the k order inside each
+//    32-block permuted by the prepack so a lane's B fragment is one 16 B load;
+//    the decode rows fill the n = 8 side of mma.sync.m16n8k16 (x^T as B).
+//  * E4M3 is widened to f16 in registers (cvt.rn.f16x2.e4m3x2).  A CUDA-core
 //    FFMA variant of the same loop (kMathFfma) exists for comparison.
-//  * Split-K partial sums are combined deterministically: per virtual tile,
-//    the warps' partials are summed in warp order by the last warp to finish
-//    it; a tile split across CTAs is summed in (k-range, CTA) order by the
-//    last CTA to arrive (a counter per tile, reset by that CTA).  No float
-//    atomics (the reference atomically adds into y_acc, gemv_fp8.cu:143-150),
-//    no memset, no separate cast kernel.
+//  * Each warp's partial per virtual tile goes to a shared-memory slot.  After
+//    the stream the slots are summed in warp order, and a tile split across
+//    CTAs is summed in (k-range, CTA) order by the last CTA to arrive (one
+//    counter per tile, reset by that CTA).  Deterministic; no float atomics
+//    (the reference atomically adds into y_acc, gemv_fp8.cu:143-150), no
+//    memset, no separate cast kernel.
 //  * Epilogues: per-channel/tensor scale, fp16 rounding, SiLU(gate)*up for the
-//    fused gate||up op, residual add; RMSNorm of the input rows in the
-//    prologue.
+//    fused gate||up op, residual add.
 #include <cstdio>
 #include <type_traits>
 
@@ -39,6 +39,14 @@ namespace b2g {
 
 __device__ int g_device_error;
 
+#ifdef B2G_TRACE
+// Per-CTA phase timestamps (%globaltimer), debug builds only.
+__device__ unsigned long long g_trace[1024][16];
+#define TRACE(i) do { g_trace[blockIdx.x][(i)] = globaltimer_ns(); } while (0)
+#else
+#define TRACE(i) do { } while (0)
+#endif
+
 int* device_error_word() {
   void* p = nullptr;
   if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
@@ -47,9 +55,8 @@ int* device_error_word() {
 
 namespace {
 
-constexpr int W = kConsumerWarps;
-constexpr int kUnitsPerWarpStage = 2;
-constexpr int kStageUnits = W * kUnitsPerWarpStage;
+constexpr int W = kWarps;
+constexpr int NT = kThreads;
 
 __device__ __forceinline__ long long cta_of(long long u, long long T, int G) {
   return ((u + 1) * G + T - 1) / T - 1;
@@ -105,14 +112,29 @@ __device__ void epilogue(const GemvParams& p, int tile, const float (&v)[P][4], 
   }
 }
 
-// A virtual tile's CTA-level partial is complete in v: finish it here if this
-// CTA is the tile's only contributor, else publish it and let the last
+// Address of the idx-th partial of output tile `tile`, contributions ordered
+// by (k-range, CTA).
+template <int P>
+__device__ __forceinline__ const float4* contrib_ptr(const GemvParams& p, int tile, int idx) {
+  const long long T = p.total_units;
+  for (int k = 0; k < p.ksplit; ++k) {
+    const long long vt = (long long)k * p.n_tiles + tile;
+    const long long a = vt * p.kbpv;
+    const int n = (int)(cta_of(a + p.kbpv - 1, T, p.grid) - cta_of(a, T, p.grid)) + 1;
+    if (idx < n)
+      return reinterpret_cast<const float4*>(p.partials) + ((size_t)vt * p.max_contrib + idx) * P * 32;
+    idx -= n;
+  }
+  return nullptr;
+}
+
+// A virtual tile's CTA-level sum is complete in v: finish it here if this CTA
+// is the tile's only contributor, else publish it and let the last
 // contributing CTA sum all partials in (k-range, CTA) order.
 template <int P>
 __device__ void finish_vt(const GemvParams& p, long long vt, const float (&v)[P][4], int lane) {
   const long long T = p.total_units;
   const int G = p.grid;
-  const int cta = blockIdx.x;
   const int ks = (int)(vt / p.n_tiles);
   const int tile = (int)(vt - (long long)ks * p.n_tiles);
   int total = 0;
@@ -126,34 +148,41 @@ __device__ void finish_vt(const GemvParams& p, long long vt, const float (&v)[P]
   }
   const long long c_first = cta_of(vt * p.kbpv, T, G);
   float4* dst = reinterpret_cast<float4*>(p.partials) +
-                ((size_t)vt * p.max_contrib + (size_t)(cta - c_first)) * P * 32;
+                ((size_t)vt * p.max_contrib + (size_t)(blockIdx.x - c_first)) * P * 32;
 #pragma unroll
   for (int pl = 0; pl < P; ++pl)
     __stcg(&dst[pl * 32 + lane], make_float4(v[pl][0], v[pl][1], v[pl][2], v[pl][3]));
-  __threadfence();
+  fence_acq_rel_gpu();
   __syncwarp();
   int old = 0;
   if (lane == 0) old = atomicAdd(&p.counters[tile], 1);
   old = __shfl_sync(0xffffffffu, old, 0);
   if (old != total - 1) return;
-  __threadfence();
+  fence_acq_rel_gpu();
   float s[P][4];
 #pragma unroll
   for (int pl = 0; pl < P; ++pl) s[pl][0] = s[pl][1] = s[pl][2] = s[pl][3] = 0.f;
-  for (int k = 0; k < p.ksplit; ++k) {
-    const long long vt2 = (long long)k * p.n_tiles + tile;
-    const long long a = vt2 * p.kbpv;
-    const long long cf = cta_of(a, T, G), cl = cta_of(a + p.kbpv - 1, T, G);
-    for (long long c = cf; c <= cl; ++c) {
-      const float4* src = reinterpret_cast<const float4*>(p.partials) +
-                          ((size_t)vt2 * p.max_contrib + (size_t)(c - cf)) * P * 32;
+  constexpr int B = 4;  // partials fetched per round trip
+  for (int base = 0; base < total; base += B) {
+    float4 t[B][P];
 #pragma unroll
-      for (int pl = 0; pl < P; ++pl) {
-        const float4 t = __ldcg(&src[pl * 32 + lane]);
-        s[pl][0] += t.x;
-        s[pl][1] += t.y;
-        s[pl][2] += t.z;
-        s[pl][3] += t.w;
+    for (int b = 0; b < B; ++b) {
+      if (base + b < total) {
+        const float4* src = contrib_ptr<P>(p, tile, base + b);
+#pragma unroll
+        for (int pl = 0; pl < P; ++pl) t[b][pl] = __ldcg(&src[pl * 32 + lane]);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      if (base + b < total) {
+#pragma unroll
+        for (int pl = 0; pl < P; ++pl) {
+          s[pl][0] += t[b][pl].x;
+          s[pl][1] += t[b][pl].y;
+          s[pl][2] += t[b][pl].z;
+          s[pl][3] += t[b][pl].w;
+        }
       }
     }
   }
@@ -162,69 +191,84 @@ __device__ void finish_vt(const GemvParams& p, long long vt, const float (&v)[P]
 }
 
 // ---------------------------------------------------------------------------
-// x (the M activation rows) -> shared memory in B-fragment order:
-// [k32 block][m][quad q][16 B], the 16 B holding, for k16 steps s = 0, 1,
-// the f16 pairs (16s + 2q, +1) and (16s + 8 + 2q, +1).
+// Activation rows in shared memory: row m at xs + m * x_rs (halves), holding
+// k in [k_lo, k_lo + krange).  The row stride is = 8 (mod 64) halves so the
+// eight rows of a B fragment fall in different banks.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void load8(const __half* row, int c, int K, bool vec, float (&f)[8]) {
-  const int k0 = c * 8;
-  if (vec && k0 + 8 <= K) {
-    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(row + k0));
-    const float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), cc = h2_to_f2(v.z), d = h2_to_f2(v.w);
-    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
-    f[4] = cc.x; f[5] = cc.y; f[6] = d.x; f[7] = d.y;
-  } else {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) f[e] = (k0 + e < K) ? __half2float(__ldcg(row + k0 + e)) : 0.f;
-  }
-}
-
-__device__ void load_x(const GemvParams& p, uint8_t* xs, int kx_lo, int nkx, float* rms_r,
-                       float* red, int tid) {
-  constexpr int NT = W * 32;
+__device__ void stage_x_manual(const GemvParams& p, __half* xs, int k_lo, int krange, int tid) {
   const int M = p.M, K = p.K;
   const bool vec = ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0) && ((p.ldx & 7) == 0);
-  if (p.rmsnorm) {
-    const int nch = (K + 7) / 8;
-    for (int m = 0; m < M; ++m) {
-      const __half* xr = p.x + (size_t)m * p.ldx;
-      float s = 0.f;
-      for (int c = tid; c < nch; c += NT) {
-        float f[8];
-        load8(xr, c, K, vec, f);
+  const int nch = krange / 8;
+  for (int idx = tid; idx < M * nch; idx += NT * 4) {
+    uint4 v[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) s = fmaf(f[e], f[e], s);
+    for (int r = 0; r < 4; ++r) {
+      const int id = idx + r * NT;
+      v[r] = make_uint4(0, 0, 0, 0);
+      if (id < M * nch) {
+        const int m = id / nch, c = id - m * nch;
+        const int k0 = k_lo + c * 8;
+        const __half* row = p.x + (size_t)m * p.ldx;
+        if (vec && k0 + 8 <= K) {
+          v[r] = __ldcg(reinterpret_cast<const uint4*>(row + k0));
+        } else {
+          uint32_t e[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) e[j] = (k0 + j < K) ? __half_as_ushort(__ldcg(row + k0 + j)) : 0u;
+          v[r] = make_uint4(e[0] | (e[1] << 16), e[2] | (e[3] << 16), e[4] | (e[5] << 16),
+                            e[6] | (e[7] << 16));
+        }
       }
+    }
 #pragma unroll
-      for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-      if ((tid & 31) == 0) red[(tid >> 5) * 8 + m] = s;
+    for (int r = 0; r < 4; ++r) {
+      const int id = idx + r * NT;
+      if (id < M * nch) {
+        const int m = id / nch, c = id - m * nch;
+        sts128(xs + (size_t)m * p.x_rs + c * 8, v[r]);
+      }
     }
-    named_sync(1, NT);
-    if (tid < M) {
-      float t = 0.f;
-      for (int w = 0; w < W; ++w) t += red[w * 8 + tid];
-      rms_r[tid] = 1.0f / sqrtf(t / (float)K + p.rms_eps);
-    }
-    named_sync(1, NT);
   }
-  const int c_lo = kx_lo * 4, nch = nkx * 4;
-  for (int idx = tid; idx < M * nch; idx += NT) {
-    const int m = idx / nch, cr = idx - m * nch;
-    float f[8];
-    load8(p.x + (size_t)m * p.ldx, c_lo + cr, K, vec, f);
-    if (p.rmsnorm) {
-      const float r = rms_r[m];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) f[e] *= r;
+}
+
+// In-place RMSNorm of the staged rows (gamma = 1): x <- fp16(x / sqrt(mean(x^2) + eps)).
+// Requires the full row in shared memory (k_lo == 0, K % 8 == 0; host-checked).
+__device__ void rmsnorm_rows(const GemvParams& p, __half* xs, float* rms_r, float* red, int tid) {
+  const int M = p.M, K = p.K;
+  const int nch = K / 8;
+  for (int m = 0; m < M; ++m) {
+    const __half* row = xs + (size_t)m * p.x_rs;
+    float s = 0.f;
+    for (int c = tid; c < nch; c += NT) {
+      const uint4 v = lds128(row + c * 8);
+      const float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), cc = h2_to_f2(v.z), d = h2_to_f2(v.w);
+      s = fmaf(a.x, a.x, s); s = fmaf(a.y, a.y, s); s = fmaf(b.x, b.x, s); s = fmaf(b.y, b.y, s);
+      s = fmaf(cc.x, cc.x, s); s = fmaf(cc.y, cc.y, s); s = fmaf(d.x, d.x, s); s = fmaf(d.y, d.y, s);
     }
-    uint32_t* base = reinterpret_cast<uint32_t*>(xs + (size_t)((cr >> 2) * M + m) * 64) + (cr & 3);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) base[j * 4] = f2_to_h2(f[2 * j], f[2 * j + 1]);
+    for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if ((tid & 31) == 0) red[(tid >> 5) * 8 + m] = s;
+  }
+  named_sync(1, NT);
+  if (tid < M) {
+    float t = 0.f;
+    for (int w = 0; w < W; ++w) t += red[w * 8 + tid];
+    rms_r[tid] = 1.0f / sqrtf(t / (float)K + p.rms_eps);
+  }
+  named_sync(1, NT);
+  for (int idx = tid; idx < M * nch; idx += NT) {
+    const int m = idx / nch, c = idx - m * nch;
+    __half* at = xs + (size_t)m * p.x_rs + c * 8;
+    const uint4 v = lds128(at);
+    const float r = rms_r[m];
+    const float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), cc = h2_to_f2(v.z), d = h2_to_f2(v.w);
+    sts128(at, make_uint4(f2_to_h2(a.x * r, a.y * r), f2_to_h2(b.x * r, b.y * r),
+                          f2_to_h2(cc.x * r, cc.y * r), f2_to_h2(d.x * r, d.y * r)));
   }
 }
 
 // ---------------------------------------------------------------------------
-// Per-unit math
+// Per-unit math.  `xk` points at the unit's first k in row 0 of the staged x.
 // ---------------------------------------------------------------------------
 template <int P, int WB>
 struct MmaMath {
@@ -233,29 +277,22 @@ struct MmaMath {
 #pragma unroll
     for (int pl = 0; pl < P; ++pl) acc[pl][0] = acc[pl][1] = acc[pl][2] = acc[pl][3] = 0.f;
   }
-  // xq = xs + (kx * M) * 64 + q * 16 (the lane's quad column of block kx)
-  __device__ __forceinline__ void unit(const uint4 (&wv)[P], const uint8_t* xq, int g, int M,
-                                       int kg) {
+  // xf: this lane's B fragment for the unit (b0..b3 for E4M3; b0, b1 for FP16).
+  __device__ __forceinline__ void unit(const uint4 (&wv)[P], const uint4& xf) {
     if constexpr (WB == 1) {
-      uint4 xb = make_uint4(0, 0, 0, 0);
-      if (g < M) xb = lds128(xq + g * 64);
 #pragma unroll
       for (int pl = 0; pl < P; ++pl) {
         const uint4 w = wv[pl];
-        mma_16816(acc[pl], e4m3x2_to_f16x2((uint16_t)(w.x & 0xFFFF)),
-                  e4m3x2_to_f16x2((uint16_t)(w.x >> 16)), e4m3x2_to_f16x2((uint16_t)(w.y & 0xFFFF)),
-                  e4m3x2_to_f16x2((uint16_t)(w.y >> 16)), xb.x, xb.y);
-        mma_16816(acc[pl], e4m3x2_to_f16x2((uint16_t)(w.z & 0xFFFF)),
-                  e4m3x2_to_f16x2((uint16_t)(w.z >> 16)), e4m3x2_to_f16x2((uint16_t)(w.w & 0xFFFF)),
-                  e4m3x2_to_f16x2((uint16_t)(w.w >> 16)), xb.z, xb.w);
+        mma_16816(acc[pl], e4m3x2_to_f16x2(w.x), e4m3x2_to_f16x2(w.x >> 16), e4m3x2_to_f16x2(w.y),
+                  e4m3x2_to_f16x2(w.y >> 16), xf.x, xf.y);
+        mma_16816(acc[pl], e4m3x2_to_f16x2(w.z), e4m3x2_to_f16x2(w.z >> 16), e4m3x2_to_f16x2(w.w),
+                  e4m3x2_to_f16x2(w.w >> 16), xf.z, xf.w);
       }
     } else {
-      uint2 xb = make_uint2(0, 0);
-      if (g < M) xb = lds64(xq + g * 64 + (kg & 1) * 8);
 #pragma unroll
       for (int pl = 0; pl < P; ++pl) {
         const uint4 w = wv[pl];
-        mma_16816(acc[pl], w.x, w.y, w.z, w.w, xb.x, xb.y);
+        mma_16816(acc[pl], w.x, w.y, w.z, w.w, xf.x, xf.y);
       }
     }
   }
@@ -278,11 +315,10 @@ struct FfmaMath {
 #pragma unroll
         for (int m = 0; m < 8; ++m) acc[pl][c][m] = 0.f;
   }
-  __device__ __forceinline__ void unit(const uint4 (&wv)[P], const uint8_t* xq, int, int M,
-                                       int kg) {
-    // weights as float pairs: wf[pl][s][r], r = (which << 1) | channel
-    constexpr int S = (WB == 1) ? 2 : 1;
-    float2 wf[P][S][4];
+  // xk: this lane's x slice of the unit in row 0 (row m at xk + m * rs).
+  __device__ __forceinline__ void unit(const uint4 (&wv)[P], const __half* xk, int M, int rs) {
+    constexpr int S = (WB == 1) ? 2 : 1;  // k16 steps per unit
+    float2 wf[P][S][4];                   // [plane][step][register r]
 #pragma unroll
     for (int pl = 0; pl < P; ++pl) {
       const uint4 w = wv[pl];
@@ -293,8 +329,7 @@ struct FfmaMath {
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
             const uint32_t word = ws[s * 2 + (r >> 1)];
-            const uint16_t pr = (r & 1) ? (uint16_t)(word >> 16) : (uint16_t)(word & 0xFFFF);
-            wf[pl][s][r] = h2_to_f2(e4m3x2_to_f16x2(pr));
+            wf[pl][s][r] = h2_to_f2(e4m3x2_to_f16x2((r & 1) ? (word >> 16) : word));
           }
       } else {
         wf[pl][0][0] = h2_to_f2(w.x);
@@ -306,17 +341,18 @@ struct FfmaMath {
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
       if (m < M) {
-        float2 xf[S][2];
+        const __half* xr = xk + (size_t)m * rs;
+        float2 xf[S][2];  // [step][which: k or k+8]
         if constexpr (WB == 1) {
-          const uint4 xv = lds128(xq + m * 64);
-          xf[0][0] = h2_to_f2(xv.x);
-          xf[0][1] = h2_to_f2(xv.y);
-          xf[1][0] = h2_to_f2(xv.z);
-          xf[1][1] = h2_to_f2(xv.w);
+          const uint4 v = lds128(xr);
+          xf[0][0] = h2_to_f2(v.x);
+          xf[0][1] = h2_to_f2(v.y);
+          xf[1][0] = h2_to_f2(v.z);
+          xf[1][1] = h2_to_f2(v.w);
         } else {
-          const uint2 xv = lds64(xq + m * 64 + (kg & 1) * 8);
-          xf[0][0] = h2_to_f2(xv.x);
-          xf[0][1] = h2_to_f2(xv.y);
+          const uint2 v = lds64(xr);
+          xf[0][0] = h2_to_f2(v.x);
+          xf[0][1] = h2_to_f2(v.y);
         }
 #pragma unroll
         for (int pl = 0; pl < P; ++pl)
@@ -362,185 +398,195 @@ struct FfmaMath {
 // The kernel
 // ---------------------------------------------------------------------------
 template <int P, int WB, int MATH>
-__global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_streamk_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr int UNIT = P * kUnitPlaneBytes;
-  const int NS = p.n_stages;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + NS;
-  int* slot_count = reinterpret_cast<int*>(smem + p.off_misc);
-  volatile int* abort_flag = slot_count + p.n_slots;
-  float* rms_r = reinterpret_cast<float*>(slot_count + p.n_slots + 1);
-  float* red = rms_r + 8;
-  uint8_t* ring = smem + p.off_ring;
-  float4* slots = reinterpret_cast<float4*>(smem + p.off_slots);
-  uint8_t* xs = smem + p.off_x;
+  // Units each lane keeps in flight: 16 B x 512 threads x D x P = 128 KB per SM.
+  constexpr int D = (MATH == kMathMma) ? (P == 1 ? 16 : 8) : (P == 1 ? 8 : 4);
+  constexpr int KPB = (WB == 1) ? 32 : 16;  // k per k-block
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(smem);
+  volatile int* abort_flag = reinterpret_cast<int*>(smem + kOffMisc);
+  float* rms_r = reinterpret_cast<float*>(smem + kOffMisc + 16);
+  float* red = reinterpret_cast<float*>(smem + 128);
+  float4* slots = reinterpret_cast<float4*>(smem + kOffSlots);  // [n_slots][W][P][32]
+  __half* xs = reinterpret_cast<__half*>(smem + p.off_x);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const long long T = p.total_units;
-  const int G = p.grid;
-  const long long u0 = (long long)blockIdx.x * T / G;
-  const long long u1 = (long long)(blockIdx.x + 1) * T / G;
-  const long long n_units = u1 - u0;
-  const int n_st = (int)((n_units + kStageUnits - 1) / kStageUnits);
-
-  if (tid == 0) {
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], W);
-    }
-    fence_mbarrier_init();
-    pdl_launch_dependents();
-  }
-  for (int i = tid; i <= p.n_slots; i += blockDim.x) slot_count[i] = 0;
-  for (int i = tid; i < p.n_slots * W * P * 32; i += blockDim.x) slots[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  __syncthreads();
-
-  if (warp == W) {
-    // ---------------- producer: TMA bulk stream of [u0, u1) ----------------
-    if (lane == 0 && n_st > 0) {
-      const uint64_t pol = l2_policy_evict_first();
-      int s = 0, err = kErrNone;
-      for (; s < n_st; ++s) {
-        const int slot = s % NS;
-        if (s >= NS && !mbar_wait_bounded(&empty[slot], ((s / NS) - 1) & 1)) {
-          err = kErrEmptyWait;
-          break;
-        }
-        if (*abort_flag) break;
-        const long long us = u0 + (long long)s * kStageUnits;
-        const int nu = (int)min((long long)kStageUnits, u1 - us);
-        const uint32_t bytes = (uint32_t)nu * UNIT;
-        mbar_arrive_expect_tx(&full[slot], bytes);
-        bulk_g2s(ring + (size_t)slot * kStageUnits * UNIT, p.packed + us * UNIT, bytes, &full[slot], pol);
-      }
-      if (err != kErrNone || *abort_flag) {
-        if (err != kErrNone) atomicCAS(p.error, 0, err);
-        *abort_flag = 1;
-        // every copy this CTA issued must land before the CTA exits
-        for (int s2 = max(0, s - NS); s2 < s; ++s2)
-          if (!mbar_wait_bounded(&full[s2 % NS], (s2 / NS) & 1)) {
-            atomicCAS(p.error, 0, kErrDrainWait);
-            break;
-          }
-      }
-    }
-    return;
-  }
-
-  // ---------------- consumers ----------------
   const int g = lane >> 2, q = lane & 3;
   const int M = p.M;
   const int kbpv = p.kbpv;
-  long long vt_first = 0;
-  int kx_lo = 0, nkx = 0;
-  if (n_units > 0) {
-    vt_first = u0 / kbpv;
-    const long long vt_last = (u1 - 1) / kbpv;
-    const int ks_lo = (int)(vt_first / p.n_tiles), ks_hi = (int)(vt_last / p.n_tiles);
-    const int kx_per_ks = kbpv * (WB == 1 ? 32 : 16) / 32;
-    kx_lo = ks_lo * kx_per_ks;
-    nkx = (ks_hi + 1) * kx_per_ks - kx_lo;
-  }
-  pdl_wait();
-  load_x(p, xs, kx_lo, nkx, rms_r, red, tid);
-  named_sync(1, W * 32);
-  if (n_units <= 0) return;
+  const long long T = p.total_units;
+  const int G = p.grid;
+  const int u0 = (int)((long long)blockIdx.x * T / G);
+  const int u1 = (int)((long long)(blockIdx.x + 1) * T / G);
+  const int n_units = u1 - u0;
+  if (n_units <= 0) return;  // whole CTA: no barrier is reached
+  if (tid == 0) TRACE(0);
+  const int n_mine = n_units > warp ? (n_units - warp + W - 1) / W : 0;  // units u0 + warp + j*W
 
-  using Math = typename std::conditional<MATH == kMathMma, MmaMath<P, WB>, FfmaMath<P, WB>>::type;
-  Math math;
-  math.zero();
-
-  // This warp's units are u0 + warp + j*W.
-  long long u = u0 + warp;
-  long long vt = u / kbpv;
-  int kbl = (int)(u - vt * kbpv);
-  int kg = (int)(vt / p.n_tiles) * kbpv + kbl;  // k-block index over padded K
-  bool touched = false;
-
-  // Flush the warp's partial for virtual tile `fvt` into its smem slot; the
-  // last warp of the CTA to do so sums the slot (warp order) and finishes it.
-  auto flush = [&](long long fvt) {
-    float v[P][4];
-    math.result(v, lane);
-    const int j = (int)(fvt - vt_first);
-    float4* sl = slots + (size_t)(j * W + warp) * P * 32;
+  // ---- weight stream: the first D units, before waiting on the previous kernel
+  const uint64_t pol = l2_policy_evict_first();
+  const uint8_t* wlane = p.packed + ((size_t)u0 + warp) * UNIT + lane * 16;
+  constexpr size_t WSTEP = (size_t)W * UNIT;
+  uint4 buf[D][P];
 #pragma unroll
-    for (int pl = 0; pl < P; ++pl) sl[pl * 32 + lane] = make_float4(v[pl][0], v[pl][1], v[pl][2], v[pl][3]);
-    __threadfence_block();
-    __syncwarp();
-    int old = 0;
-    if (lane == 0) old = atomicAdd(&slot_count[j], 1);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    const long long a = max(fvt * kbpv, u0), b = min((fvt + 1) * kbpv, u1);
-    const int expected = (int)min((long long)W, b - a);
-    if (old == expected - 1) {
-      __threadfence_block();
-      float s[P][4];
+  for (int d = 0; d < D; ++d)
+    if (d < n_mine) {
 #pragma unroll
-      for (int pl = 0; pl < P; ++pl) s[pl][0] = s[pl][1] = s[pl][2] = s[pl][3] = 0.f;
-      for (int w = 0; w < W; ++w) {
-        const float4* src = slots + (size_t)(j * W + w) * P * 32;
-#pragma unroll
-        for (int pl = 0; pl < P; ++pl) {
-          const float4 t = src[pl * 32 + lane];
-          s[pl][0] += t.x;
-          s[pl][1] += t.y;
-          s[pl][2] += t.z;
-          s[pl][3] += t.w;
-        }
-      }
-      finish_vt<P>(p, fvt, s, lane);
+      for (int pl = 0; pl < P; ++pl) buf[d][pl] = ldg_stream(wlane + d * WSTEP + pl * kUnitPlaneBytes, pol);
     }
-  };
 
-  for (int s = 0; s < n_st; ++s) {
-    const int slot = s % NS;
-    const bool ok = mbar_wait_bounded(&full[slot], (s / NS) & 1);
-    if (!__all_sync(0xffffffffu, ok)) {
+  if (tid == 0) {
+    mbar_init(xbar, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    pdl_launch_dependents();
+  }
+  for (int i = tid; i < p.n_slots * W * P * 32; i += NT) slots[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  // ---- the x rows this CTA needs
+  const int vt_first = u0 / kbpv;
+  const int vt_last = (u1 - 1) / kbpv;
+  const int ks_lo = vt_first / p.n_tiles, ks_hi = vt_last / p.n_tiles;
+  const int k_lo = ks_lo * kbpv * KPB;
+  const int krange = (ks_hi + 1 - ks_lo) * kbpv * KPB;
+  __syncthreads();
+  pdl_wait();
+  if (tid == 0) TRACE(1);
+  if (p.x_tma) {
+    if (tid == 0) {
+      fence_proxy_async_global();
+      const uint32_t row_bytes = (uint32_t)krange * 2;
+      mbar_arrive_expect_tx(xbar, row_bytes * M);
+      const uint64_t keep = l2_policy_evict_last();
+      for (int m = 0; m < M; ++m)
+        bulk_g2s(xs + (size_t)m * p.x_rs, p.x + (size_t)m * p.ldx + k_lo, row_bytes, xbar, keep);
+    }
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(xbar, 0))) {
       if (lane == 0) {
         atomicCAS(p.error, 0, kErrFullWait);
         *abort_flag = 1;
       }
-      return;
     }
-    const long long us = u0 + (long long)s * kStageUnits;
-    const int nu = (int)min((long long)kStageUnits, u1 - us);
-    const uint8_t* stage = ring + (size_t)slot * kStageUnits * UNIT;
-    uint4 wv[kUnitsPerWarpStage][P];
+  } else {
+    stage_x_manual(p, xs, k_lo, krange, tid);
+  }
+  __syncthreads();
+  if (p.rmsnorm) {
+    rmsnorm_rows(p, xs, rms_r, red, tid);
+    __syncthreads();
+  }
+  if (tid == 0) TRACE(2);
+
+  // ---- stream: compute unit j while units j+1 .. j+D-1 are in flight
+  using Math = typename std::conditional<MATH == kMathMma, MmaMath<P, WB>, FfmaMath<P, WB>>::type;
+  Math math;
+  math.zero();
+  // Segment bookkeeping: this warp's units in the current virtual tile are
+  // counted down (seg_left) instead of re-deriving the tile per unit.
+  int vt = (u0 + warp) / kbpv;
+  int kbl = (u0 + warp) - vt * kbpv;  // k-block (within vt) of the segment's first unit
+  int seg_n = (kbpv - kbl + W - 1) / W;  // this warp's units in vt
+  int seg_left = seg_n;
+  int cur_j = vt - vt_first;
+  // This lane's slice of the staged x: the prepack permutes k inside each
+  // block so the B fragment is one 16 B (E4M3) or 8 B (FP16) load at
+  // k-offset 8q (4q) of row g.  xoff: k offset of the warp's next unit.
+  const __half* xlane = xs + (size_t)(g < M ? g : 0) * p.x_rs + (WB == 1 ? 8 * q : 4 * q);
+  const __half* xq = xs + (WB == 1 ? 8 * q : 4 * q);  // row 0, for the FFMA variant
+  int xoff = ((vt / p.n_tiles) * kbpv + kbl) * KPB - k_lo;
+  const uint8_t* lp = wlane + D * WSTEP;  // address of unit j + D
+  int loads_left = n_mine - D;
+
+  auto flush = [&](int j) {
+    float v[P][4];
+    math.result(v, lane);
 #pragma unroll
-    for (int jj = 0; jj < kUnitsPerWarpStage; ++jj) {
-      const int i = warp + jj * W;
-      if (i < nu) {
+    for (int pl = 0; pl < P; ++pl)
+      slots[((size_t)(j * W + warp) * P + pl) * 32 + lane] = make_float4(v[pl][0], v[pl][1], v[pl][2], v[pl][3]);
+  };
+
+  for (int j0 = 0; j0 < n_mine; j0 += D) {
 #pragma unroll
-        for (int pl = 0; pl < P; ++pl) wv[jj][pl] = lds128(stage + (size_t)i * UNIT + pl * kUnitPlaneBytes + lane * 16);
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
+    for (int d = 0; d < D; ++d) {
+      if (j0 + d < n_mine) {
+        uint4 xf = make_uint4(0, 0, 0, 0);
+        if constexpr (MATH == kMathMma) {
+          if (g < M) {
+            if constexpr (WB == 1) {
+              xf = lds128(xlane + xoff);
+            } else {
+              const uint2 t = lds64(xlane + xoff);
+              xf.x = t.x;
+              xf.y = t.y;
+            }
+          }
+          math.unit(buf[d], xf);
+        } else {
+          math.unit(buf[d], xq + xoff, M, p.x_rs);
+        }
+        if (loads_left > 0) {
 #pragma unroll
-    for (int jj = 0; jj < kUnitsPerWarpStage; ++jj) {
-      const int i = warp + jj * W;
-      if (i < nu) {
-        const int kx = (WB == 1 ? kg : (kg >> 1)) - kx_lo;
-        math.unit(wv[jj], xs + (size_t)kx * M * 64 + q * 16, g, M, kg);
-        touched = true;
-        kbl += W;
-        kg += W;
-        if (kbl >= kbpv) {
-          flush(vt);
+          for (int pl = 0; pl < P; ++pl) buf[d][pl] = ldg_stream(lp + pl * kUnitPlaneBytes, pol);
+          lp += WSTEP;
+        }
+        --loads_left;
+        xoff += W * KPB;
+        if (--seg_left == 0) {
+          // this warp's next virtual tile: unit vt*kbpv + kbl + seg_n*W
+          flush(cur_j);
           math.zero();
-          touched = false;
-          do {
+          kbl += seg_n * W - kbpv;
+          ++vt;
+          while (kbl >= kbpv) {
             kbl -= kbpv;
             ++vt;
-          } while (kbl >= kbpv);
-          kg = (int)(vt / p.n_tiles) * kbpv + kbl;
+          }
+          seg_n = (kbpv - kbl + W - 1) / W;
+          seg_left = seg_n;
+          cur_j = vt - vt_first;
+          xoff = ((vt / p.n_tiles) * kbpv + kbl) * KPB - k_lo;
         }
       }
     }
   }
-  if (touched) flush(vt);
+  if (n_mine > 0 && seg_left != seg_n) flush(cur_j);
+  if (tid == 0) {
+    TRACE(3);
+    // Warm L2 with the start of the range the next kernel's CTA of the same
+    // index will stream.
+    if (p.pf_packed != nullptr && (int)blockIdx.x < p.pf_grid) {
+      const long long a = (long long)blockIdx.x * p.pf_total_units / p.pf_grid;
+      const long long b = (long long)(blockIdx.x + 1) * p.pf_total_units / p.pf_grid;
+      const long long bytes = min((long long)p.pf_bytes, (b - a) * p.pf_unit_bytes);
+      const uint8_t* src = p.pf_packed + a * p.pf_unit_bytes;
+      for (long long off = 0; off < bytes; off += 32768)
+        bulk_prefetch_l2(src + off, (uint32_t)min(32768LL, bytes - off));
+    }
+  }
+
+  // ---- combine: the warps' partials in warp order, then finish each tile
+  __syncthreads();
+  if (*abort_flag) return;
+  const int nvt = vt_last - vt_first + 1;
+  for (int j = warp; j < nvt; j += W) {
+    float v[P][4];
+#pragma unroll
+    for (int pl = 0; pl < P; ++pl) v[pl][0] = v[pl][1] = v[pl][2] = v[pl][3] = 0.f;
+    for (int w = 0; w < W; ++w) {
+#pragma unroll
+      for (int pl = 0; pl < P; ++pl) {
+        const float4 t = slots[((size_t)(j * W + w) * P + pl) * 32 + lane];
+        v[pl][0] += t.x;
+        v[pl][1] += t.y;
+        v[pl][2] += t.z;
+        v[pl][3] += t.w;
+      }
+    }
+    finish_vt<P>(p, vt_first + j, v, lane);
+  }
+  if (tid == 0) TRACE(4);
 }
 
 template <int P, int WB, int MATH>
@@ -581,6 +627,13 @@ cudaError_t launch_gemv(const GemvParams& p, int planes, int wbytes, int math, s
 #undef B2G_CASE
   return cudaErrorInvalidValue;
 }
+
+#ifdef B2G_TRACE
+extern "C" int b2g_debug_trace(unsigned long long* out, int n_ctas) {
+  return (int)cudaMemcpyFromSymbol(out, g_trace, sizeof(unsigned long long) * 16 * n_ctas);
+}
+
+#endif
 
 cudaError_t gemv_set_smem_limit(int bytes) {
   cudaError_t e = cudaSuccess, r;

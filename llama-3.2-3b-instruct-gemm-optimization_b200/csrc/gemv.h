@@ -15,11 +15,22 @@ namespace b2g {
 //   A "tile" is 16 output channels.  K is cut into `ksplit` equal k-ranges;
 //   a "virtual tile" (vt) is one tile over one k-range.  The stream is ordered
 //   [ks][tile][kb-in-range][plane][lane][16 B], so every CTA streams one
-//   contiguous byte range: units [u0, u1) with u0 = cta * T / grid.
+//   contiguous byte range: units [u0, u1) with u0 = cta * T / grid, which
+//   its warps stream round-robin (warp w takes units u0 + w + j * kWarps).
 constexpr int kUnitPlaneBytes = 512;
 constexpr int kTileCh = 16;
-constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kWarps = 16;  // one CTA of 16 warps per SM
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxSlots = 8;  // virtual tiles one CTA may touch
+// Shared memory: [0,8) x barrier, [64,80) flags, [80,112) RMS factors,
+// [128,640) RMSNorm partial sums, then the per-warp partial slots
+// [n_slots][warps][planes][32 lanes][16 B], then the x rows.
+constexpr int kOffMisc = 64;
+constexpr int kOffSlots = 1024;
+// Workspace: tile counters first (fixed size, so ops sharing one workspace
+// agree on where they are), then the split-K partials.
+constexpr int kCounterRegionBytes = 65536;
+constexpr int kMaxTiles = kCounterRegionBytes / 4;
 
 enum MathKind : int { kMathMma = 0, kMathFfma = 1 };
 
@@ -33,7 +44,7 @@ struct GemvParams {
   __half* y;
   long long ldy;
   float* partials;  // [n_vt][max_contrib][planes][32 lanes][4]
-  int* counters;    // [n_tiles]
+  int* counters;    // [n_tiles], zero between calls
   int* error;
   long long total_units;
   int grid;
@@ -47,11 +58,17 @@ struct GemvParams {
   int residual_add;
   float rms_eps;
   int max_contrib;
-  int n_slots;
-  int xk_cap;  // k32 blocks of x held in shared memory
-  int stage_units;
-  int n_stages;
-  int off_misc, off_ring, off_slots, off_x;  // shared-memory byte offsets
+  int n_slots;    // max virtual tiles per CTA (<= kMaxSlots)
+  int off_x;      // shared-memory byte offset of the x rows
+  int x_rs;       // x row stride in shared memory (halves)
+  int x_tma;      // 1: stage x with bulk copies (aligned rows, K % 32 == 0)
+  // L2 prefetch of the next kernel's stream: CTA c prefetches the first
+  // pf_bytes of the range the next kernel's CTA c will stream (0 = off).
+  const uint8_t* pf_packed;
+  long long pf_total_units;
+  int pf_unit_bytes;
+  int pf_grid;
+  int pf_bytes;
 };
 
 // Launch one GEMV (planes = 1 or 2, wbytes = 1 for E4M3 or 2 for FP16).

@@ -30,23 +30,27 @@ __global__ void prepack_kernel(const uint8_t* __restrict__ w, long long ld, int 
   const int g = lane >> 2, q = lane & 3;
   uint8_t out[16];
   if (wbytes == 1) {
-    // byte j: pair pr = j/2 (element e = j%2) -> k16 step s = pr/4, register
-    // r = pr%4: channel g + 8*(r&1), k = 32kb + 16s + 2q + 8*(r>>1) + e.
+    // Byte j: A-register pair pr = j/2 (element e = j%2) -> k16 step s = pr/4,
+    // register r = pr%4: channel g + 8*(r&1), MMA k-slot 16s + 8*(r>>1) + 2q + e.
+    // Slots are mapped to k inside the 32-block so that lane q's B fragment is
+    // x[8q .. 8q+7]: k = 32kb + 8q + 4s + 2*(r>>1) + e.
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int pr = j >> 1, e = j & 1, s = pr >> 2, r = pr & 3;
       const int n = tile * kTileCh + g + 8 * (r & 1);
-      const int k = kb * 32 + 16 * s + 2 * q + 8 * (r >> 1) + e;
+      const int k = kb * 32 + 8 * q + 4 * s + 2 * (r >> 1) + e;
       out[j] = (k < K && n < N) ? w[widx(layout, ld, k, n)] : 0;
     }
   } else {
-    // half j: register r = j/2, element e = j%2 of one k16 step.
+    // half j: register r = j/2, element e = j%2 of one k16 step; k-slot
+    // 8*(r>>1) + 2q + e maps to k = 16kb + 4q + 2*(r>>1) + e, so lane q's B
+    // fragment is x[4q .. 4q+3].
     const uint16_t* w16 = reinterpret_cast<const uint16_t*>(w);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int r = j >> 1, e = j & 1;
       const int n = tile * kTileCh + g + 8 * (r & 1);
-      const int k = kb * 16 + 2 * q + 8 * (r >> 1) + e;
+      const int k = kb * 16 + 4 * q + 2 * (r >> 1) + e;
       const uint16_t v = (k < K && n < N) ? w16[widx(layout, ld, k, n)] : 0;
       out[2 * j] = (uint8_t)(v & 0xFF);
       out[2 * j + 1] = (uint8_t)(v >> 8);

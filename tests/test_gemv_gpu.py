@@ -100,10 +100,11 @@ def test_gemv_parity(b2g, orc, syn, cuda, K, N, wd, mode):
 @pytest.mark.parametrize("K,N", [(3072, 8192), (200, 120)])
 def test_gemv_nk_layout(b2g, orc, syn, cuda, K, N):
     for wd in (0, 1):
-        Wd, Wh, s = make_weights(orc, syn, 32, K, N, wd, 3, layout=1)
+        mode = 3 if wd else 0
+        Wd, Wh, s = make_weights(orc, syn, 32, K, N, wd, mode, layout=1)
         x = syn.activations(7, 8, K)
-        _, _, y = run_op(b2g, K, N, wd, 3, dev(x), Wd, s, layout=1)
-        want = orc.gemv(Wh, orc.WTYPE_FP8 if wd else orc.WTYPE_FP16, x, 3, s, orc.LAYOUT_NK)
+        _, _, y = run_op(b2g, K, N, wd, mode, dev(x), Wd, s, layout=1)
+        want = orc.gemv(Wh, orc.WTYPE_FP8 if wd else orc.WTYPE_FP16, x, mode, s, orc.LAYOUT_NK)
         check(orc, y, want, wd)
 
 
@@ -144,9 +145,9 @@ def test_unaligned_rows_and_strides(b2g, orc, syn, cuda):
 # --------------------------------------------------------------------------
 # Stream-K properties
 # --------------------------------------------------------------------------
-@pytest.mark.parametrize("grid", [37, 74, 148, 296, 500])
-def test_grid_partitions(b2g, orc, syn, cuda, grid):
-    K, N = 8192, 3072
+@pytest.mark.parametrize("K,N,grid", [(8192, 3072, 148), (8192, 3072, 160), (8192, 3072, 296),
+                                      (8192, 3072, 500), (3072, 8192, 120), (3072, 8192, 296)])
+def test_grid_partitions(b2g, orc, syn, cuda, K, N, grid):
     Wd, Wh, s = make_weights(orc, syn, 34, K, N, 1, 3)
     x = syn.activations(10, 8, K)
     _, _, y = run_op(b2g, K, N, 1, 3, dev(x), Wd, s, options={b2g.OPT_GRID: grid})
@@ -171,8 +172,7 @@ def test_deterministic_and_rows_independent(b2g, orc, syn, cuda):
         torch.cuda.synchronize()
         assert torch.equal(ym[0], y1[m])
     # the kernels leave the tile counters at zero
-    nb = op.workspace_bytes()
-    counters = ws[nb - ((op.plan(8)["n_tiles"] + 63) // 64 * 256):].view(torch.int32)
+    counters = ws[:op.plan(8)["n_tiles"] * 4].view(torch.int32)
     assert int(counters.abs().sum()) == 0
     assert b2g.device_error() == 0
 
