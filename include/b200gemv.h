@@ -40,7 +40,9 @@ typedef enum {
   B2G_ERR_CUDA = 3,         /* a CUDA runtime call failed */
   B2G_ERR_PEER_TIMEOUT = 4, /* a device-side wait on a peer gave up */
   B2G_ERR_OOM = 5,          /* shared memory or workspace too small */
-  B2G_ERR_DEVICE = 6        /* a kernel recorded an error (bounded wait expired) */
+  B2G_ERR_DEVICE = 6,       /* a kernel recorded an error (bounded wait expired) */
+  B2G_ERR_SCRATCH_LIMIT = 7 /* b2g_enqueue_static: the call needs more than
+                               B2G_STATIC_SCRATCH_BYTES of workspace */
 } b2g_status;
 
 /* Weight element type (reference: FP16 kernels/gemv_fp16.cu, E4M3 kernels/gemv_fp8.cu). */
@@ -188,6 +190,34 @@ b2g_status b2g_enqueue_ex(const b2g_op* op, const b2g_enqueue_args* args, b2g_st
 /* Reads (and optionally clears) the device error word that kernels set when
  * a bounded wait expires.  Synchronises the current device. */
 b2g_status b2g_device_error(int32_t* code, int32_t clear);
+
+/* ------------------------------------------------------------------------
+ * No-allocation enqueue.  No counterpart in the reference (its run_gemv takes
+ * a caller-allocated y_acc, kernels/gemv_fp8.cu:276-283).
+ *
+ * Same computation and arguments as b2g_enqueue_ex, except that
+ * args->workspace must be NULL: the workspace is a fixed array of
+ * B2G_STATIC_SCRATCH_BYTES compiled into the library (one per device), so
+ * the call itself allocates nothing, on the device or the host.  It is for
+ * callers that cannot allocate at enqueue time: a plugin whose engine
+ * granted it no workspace, a process whose device memory is all handed to
+ * another allocator's pool up front, or a latency-bound loop that must not
+ * reach cudaFree (which synchronises the device).
+ *  - Limit: a call whose b2g_workspace_size exceeds B2G_STATIC_SCRATCH_BYTES
+ *    returns B2G_ERR_SCRATCH_LIMIT and launches nothing.  2 MiB covers every
+ *    Llama-3.2-3B MLP op (the largest, fused gate||up, needs 1.06 MiB).
+ *  - Zeroing: the tile counters at the start of the scratch must be zero
+ *    when the kernel starts; this call clears them on `stream` before every
+ *    launch (the split-K partials need no clearing).
+ *  - Races: the scratch is shared by every call on the device.  Calls that
+ *    can run at the same time -- on different streams, or from different
+ *    host threads -- race on it and give wrong results.  Calls in one stream
+ *    are ordered and safe.
+ *  - args->pdl is ignored (launched without programmatic dependent launch,
+ *    so the counter clearing is complete before the kernel starts).
+ * ------------------------------------------------------------------------ */
+#define B2G_STATIC_SCRATCH_BYTES (2u * 1024u * 1024u)
+b2g_status b2g_enqueue_static(const b2g_op* op, const b2g_enqueue_args* args, b2g_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Decode MLP stack: n_layers x [RMSNorm -> fused gate||up + SiLU*up -> down +

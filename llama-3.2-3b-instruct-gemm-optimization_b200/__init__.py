@@ -19,7 +19,8 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libb200gemv.so"
 
-OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_PEER_TIMEOUT, ERR_OOM, ERR_DEVICE = range(7)
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_PEER_TIMEOUT, ERR_OOM, ERR_DEVICE, ERR_SCRATCH_LIMIT = range(8)
+STATIC_SCRATCH_BYTES = 2 * 1024 * 1024  # B2G_STATIC_SCRATCH_BYTES
 DTYPE = {"fp16": 0, "fp8_e4m3": 1}
 SCALE = {"none": 0, "tensor_fp16": 1, "channel_fp16": 2, "channel_fp32": 3}
 LAYOUT = {"KN": 0, "NK": 1}
@@ -85,6 +86,7 @@ SIGNATURES = {
     "b2g_enqueue": ([_P, _I32, _P, _P, _P, _P, _P, _P], ctypes.c_int),
     "b2g_enqueue_ex": ([_P, ctypes.POINTER(EnqueueArgs), _P], ctypes.c_int),
     "b2g_device_error": ([ctypes.POINTER(_I32), _I32], ctypes.c_int),
+    "b2g_enqueue_static": ([_P, ctypes.POINTER(EnqueueArgs), _P], ctypes.c_int),
     "b2g_stack_create": ([ctypes.POINTER(StackFields), ctypes.POINTER(_P)], ctypes.c_int),
     "b2g_stack_destroy": ([_P], ctypes.c_int),
     "b2g_stack_ops": ([_P, ctypes.POINTER(_P), ctypes.POINTER(_P)], ctypes.c_int),
@@ -220,6 +222,23 @@ class GemvOp:
                         None if prefetch is None else prefetch[1].data_ptr(),
                         None if prefetch is None else prefetch[0].h)
         check(lib().b2g_enqueue_ex(self.h, ctypes.byref(a), _stream(stream)), "b2g_enqueue_ex")
+        return y
+
+    def enqueue_static(self, x, packed, y, scales=None, residual=None, rms_eps: float = 1e-5,
+                       stream=None):
+        """y = op(x, W, scales) on the library's static scratch (b2g_enqueue_static).
+
+        The library call allocates nothing, so y must be given.  Calls that
+        overlap on the device (other streams or threads) race on the scratch.
+        """
+        if x.stride(-1) != 1 or y.stride(-1) != 1 or (residual is not None and residual.stride(-1) != 1):
+            raise ValueError("x, y and residual rows must be contiguous")
+        a = EnqueueArgs(x.shape[0], x.data_ptr(), _rows_stride(x), packed.data_ptr(),
+                        0 if scales is None else scales.data_ptr(),
+                        0 if residual is None else residual.data_ptr(),
+                        0 if residual is None else _rows_stride(residual), y.data_ptr(),
+                        _rows_stride(y), None, rms_eps, 0, None, None)
+        check(lib().b2g_enqueue_static(self.h, ctypes.byref(a), _stream(stream)), "b2g_enqueue_static")
         return y
 
 

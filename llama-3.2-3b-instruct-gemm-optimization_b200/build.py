@@ -15,7 +15,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 LIB = HERE / "libb200gemv.so"
-SOURCES = ["gemv.cu", "pack.cu", "api.cpp"]
+SOURCES = ["gemv.cu", "pack.cu", "static_scratch.cu", "api.cpp"]
 HEADERS = ["device.cuh", "gemv.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

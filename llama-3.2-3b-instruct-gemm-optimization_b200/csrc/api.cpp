@@ -136,6 +136,7 @@ const char* b2g_status_string(b2g_status s) {
     case B2G_ERR_PEER_TIMEOUT: return "peer wait timed out";
     case B2G_ERR_OOM: return "out of shared memory or workspace";
     case B2G_ERR_DEVICE: return "device-side error";
+    case B2G_ERR_SCRATCH_LIMIT: return "call needs more workspace than the static scratch (B2G_STATIC_SCRATCH_BYTES)";
   }
   return "unknown status";
 }
@@ -404,6 +405,40 @@ b2g_status b2g_device_error(int32_t* code, int32_t clear) {
   *code = v;
   if (clear && cudaMemset(w, 0, sizeof(int)) != cudaSuccess) return B2G_ERR_CUDA;
   return B2G_OK;
+}
+
+// ---------------------------------------------------------------------------
+// No-allocation enqueue: b2g_enqueue_ex over the library's static scratch
+// ---------------------------------------------------------------------------
+static void* g_static_ws[64];  // scratch address per device, under g_mu
+
+b2g_status b2g_enqueue_static(const b2g_op* op, const b2g_enqueue_args* args, b2g_stream_t stream) {
+  if (!op || !args || args->workspace) return B2G_ERR_INVALID;
+  size_t need = 0;
+  b2g_status st = b2g_workspace_size(op, args->m, &need);
+  if (st != B2G_OK) return st;
+  if (need > B2G_STATIC_SCRATCH_BYTES) return B2G_ERR_SCRATCH_LIMIT;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B2G_ERR_CUDA;
+  if (dev != op->device || dev < 0 || dev >= 64) return B2G_ERR_INVALID;
+  void* ws = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_static_ws[dev]) {
+      void* p = nullptr;
+      if (static_scratch_address(&p) != cudaSuccess || !p) return B2G_ERR_CUDA;
+      g_static_ws[dev] = p;
+    }
+    ws = g_static_ws[dev];
+  }
+  // The tile counters must start at zero; nothing else in the scratch must.
+  if (cudaMemsetAsync(ws, 0, (size_t)op->n_tiles * sizeof(int), reinterpret_cast<cudaStream_t>(stream)) !=
+      cudaSuccess)
+    return B2G_ERR_CUDA;
+  b2g_enqueue_args a = *args;
+  a.workspace = ws;
+  a.pdl = 0;
+  return b2g_enqueue_ex(op, &a, stream);
 }
 
 // ---------------------------------------------------------------------------

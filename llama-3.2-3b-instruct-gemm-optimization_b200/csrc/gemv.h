@@ -85,5 +85,8 @@ cudaError_t launch_quantize(const __half* w16, int K, int N, int layout, int sca
                             uint8_t* w8, void* scales, cudaStream_t stream);
 
 int* device_error_word();  // address of the library's device error word (current device)
+// Device address of the fixed scratch used by b2g_enqueue_static (current
+// device; static_scratch.cu).
+cudaError_t static_scratch_address(void** ptr);
 
 }  // namespace b2g

@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol(b2g):
 def test_status_strings_and_version(b2g):
     L = b2g.lib()
     assert L.b2g_version() >= 100
-    for s in range(7):
+    for s in range(8):
         assert L.b2g_status_string(s)
     assert L.b2g_status_string(0) == b"ok"
 
@@ -67,6 +67,7 @@ def test_null_arguments_rejected(b2g):
     n = ctypes.c_size_t()
     assert L.b2g_prepack_size(None, ctypes.byref(n)) == b2g.ERR_INVALID
     assert L.b2g_enqueue_ex(None, None, None) == b2g.ERR_INVALID
+    assert L.b2g_enqueue_static(None, None, None) == b2g.ERR_INVALID
     assert L.b2g_quantize_e4m3(None, 4, 4, 0, 0, None, None, None) == b2g.ERR_INVALID
     assert L.b2g_stack_create(None, None) == b2g.ERR_INVALID
     assert L.b2g_destroy(None) == b2g.OK
