@@ -208,11 +208,20 @@ def run_ours(args):
     tp = world
     M = args.m
     inter = INTER // tp
-    gu_op = b2g.GemvOp(HIDDEN, inter, max_m=M,
-                       fuse=b2g.FUSE_GATE_UP_SILU | b2g.FUSE_RMSNORM_INPUT)
-    dn_op = b2g.GemvOp(inter, HIDDEN, max_m=M,
-                       fuse=b2g.FUSE_RESIDUAL_ADD if rank == 0 else b2g.FUSE_NONE)
+    if tp == 1:
+        # One GPU: the library's stack (one cooperative launch for all layers).
+        st = b2g.Stack(HIDDEN, INTER, LAYERS, max_m=M)
+        gu_op, dn_op = st.gate_up, st.down
+    else:
+        st = None
+        gu_op = b2g.GemvOp(HIDDEN, inter, max_m=M,
+                           fuse=b2g.FUSE_GATE_UP_SILU | b2g.FUSE_RMSNORM_INPUT)
+        dn_op = b2g.GemvOp(inter, HIDDEN, max_m=M,
+                           fuse=b2g.FUSE_RESIDUAL_ADD if rank == 0 else b2g.FUSE_NONE)
     layers = make_layers(b2g, torch, device, tp, rank, (gu_op, dn_op), M)
+    if st is not None:
+        for i, L in enumerate(layers):
+            st.set_layer(i, L["pgu"], L["sgu"], L["pd"], L["sd"])
     torch.cuda.synchronize()
 
     stream = torch.cuda.current_stream()
@@ -225,7 +234,7 @@ def run_ours(args):
                      device=device)
     ws.zero_()
 
-    def step():
+    def step_ops():
         for i, L in enumerate(layers):
             nxt = layers[(i + 1) % LAYERS]
             gu_op.enqueue(h, L["pgu"], L["sgu"], y=act, workspace=ws, pdl=True,
@@ -235,7 +244,11 @@ def run_ours(args):
             if tp > 1:
                 dist.all_reduce(h)
 
-    launches_per_step = 2 * LAYERS
+    def step_stack():
+        st.enqueue(h, act, ws)
+
+    step = step_stack if st is not None else step_ops
+    launches_per_step = (LAYERS + 31) // 32 if st is not None else 2 * LAYERS
 
     # CUDA graph of one step (the serving path); direct launches as a fallback
     graph = None
@@ -286,28 +299,53 @@ def run_ours(args):
     ms_step = ms / args.steps
     value = bytes_rank * tp / (ms_step * 1e-3) / 1e12
 
-    # ---- dominant kernel: fused RMSNorm + gate||up + SiLU*up, 28 layers back to back
+    hbm, peak_kind = peaks()
+    reps = max(5, args.steps // 20)
+    detail_extra = {}
+    if st is not None:
+        # The per-layer launch path of the same stack, for comparison.
+        st.set_mode("per_layer")
+        for _ in range(3):
+            step_stack()
+        ms_pl = timed(step_stack, reps) / reps
+        st.set_mode("persistent")
+        detail_extra["per_layer_launches_ms_per_step"] = round(ms_pl, 5)
+        detail_extra["per_layer_launches_us_per_layer"] = round(ms_pl * 1e3 / LAYERS, 3)
+
+    # ---- dominant kernel.  One GPU: the stack kernel is the step's only
+    # launch, so its duration is the graph replay time per step.
+    if st is not None:
+        achieved = bytes_rank / (ms_step * 1e-3) / 1e9
+        traffic = None
+        tf = ROOT / "profiles" / "traffic.json"
+        if tf.exists():
+            traffic = json.loads(tf.read_text()).get(f"stack_m{M}")
+        roofline = {"kernel": "stack_kernel<1> (28 layers: RMSNorm + gate||up + SiLU*up, down + residual)",
+                    "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                    "frac": round(achieved / hbm, 4), "traffic": traffic,
+                    "peak_source": f"{peak_kind} hbm_gbs (STREAM-style copy)",
+                    "alg_bytes_per_launch": bytes_rank,
+                    "us_per_launch": round(ms_step * 1e3, 3)}
+
+    # ---- per-op kernels: fused RMSNorm + gate||up + SiLU*up, 28 layers back to back
     def gu_sweep():
         for i, L in enumerate(layers):
             gu_op.enqueue(h, L["pgu"], L["sgu"], y=act, workspace=ws, pdl=True,
                           prefetch=(gu_op, layers[(i + 1) % LAYERS]["pgu"]))
     for _ in range(3):
         gu_sweep()
-    reps = max(5, args.steps // 20)
     ms_gu = timed(gu_sweep, reps) / (reps * LAYERS)
-    hbm, peak_kind = peaks()
-    achieved = gu_b / (ms_gu * 1e-3) / 1e9
-    traffic = None
-    tf = ROOT / "profiles" / "traffic.json"
-    if tf.exists():
-        t = json.loads(tf.read_text()).get(f"gate_up_m{M}_tp{tp}")
-        traffic = t
-    roofline = {"kernel": "gemv_streamk_kernel<2,1,0> (RMSNorm + gate||up + SiLU*up)",
-                "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                "frac": round(achieved / hbm, 4), "traffic": traffic,
-                "peak_source": f"{peak_kind} hbm_gbs", "alg_bytes_per_launch": gu_b,
-                "us_per_launch": round(ms_gu * 1e3, 3)}
-    ms_dn = None
+    if st is None:
+        achieved = gu_b / (ms_gu * 1e-3) / 1e9
+        traffic = None
+        tf = ROOT / "profiles" / "traffic.json"
+        if tf.exists():
+            traffic = json.loads(tf.read_text()).get(f"gate_up_m{M}_tp{tp}")
+        roofline = {"kernel": "gemv_streamk_kernel<2,1,0> (RMSNorm + gate||up + SiLU*up)",
+                    "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                    "frac": round(achieved / hbm, 4), "traffic": traffic,
+                    "peak_source": f"{peak_kind} hbm_gbs (STREAM-style copy)",
+                    "alg_bytes_per_launch": gu_b, "us_per_launch": round(ms_gu * 1e3, 3)}
 
     def dn_sweep():
         for i, L in enumerate(layers):
@@ -361,12 +399,17 @@ def run_ours(args):
             "roofline": roofline,
             "e2e": {"value": round(e2e_value, 4), "unit": "TB/s", "h2d_bytes_per_step": 2 * M * HIDDEN,
                     "d2h_bytes_per_step": 2 * M * HIDDEN, "ms_per_step": round(ms_e2e, 5),
-                    "path": "pinned host h -> b2g C ABI enqueues (56 launches) -> pinned host h"},
+                    "path": ("pinned host h -> b2g_stack_enqueue (C ABI) -> pinned host h" if st is not None
+                             else "pinned host h -> b2g_enqueue_ex per layer + NCCL all-reduce -> pinned host h")},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
             "detail": {
+                **detail_extra,
                 "direct_launch_ms_per_step": round(ms_direct / args.steps, 5),
+                "gate_up_us_per_launch": round(ms_gu * 1e3, 3),
+                "gate_up_alg_bytes": gu_b,
+                "gate_up_achieved_gbs": round(gu_b / (ms_gu * 1e-3) / 1e9, 1),
                 "down_us_per_launch": round(ms_dn * 1e3, 3),
                 "down_alg_bytes": dn_b,
                 "down_achieved_gbs": round(dn_b / (ms_dn * 1e-3) / 1e9, 1),

@@ -112,9 +112,10 @@ typedef struct {
                              y and workspace are safe: they are touched only
                              after the wait). */
   const void* prefetch_packed; /* optional: packed weights of the kernel that
-                                  will follow this one in the stream; once its
-                                  own stream is issued, each CTA warms L2 with
-                                  the start of that kernel's range (NULL = off) */
+                                  will follow this one in the stream; at its
+                                  start each CTA asks L2 to fetch the range
+                                  that kernel's CTA of the same index will
+                                  stream (NULL = off) */
   const struct b2g_op* prefetch_op; /* the op prefetch_packed belongs to */
 } b2g_enqueue_args;
 
@@ -249,9 +250,20 @@ b2g_status b2g_stack_set_layer(b2g_stack* st, int32_t layer, const void* packed_
                                const void* scales_down);
 b2g_status b2g_stack_workspace_size(const b2g_stack* st, int32_t m, size_t* bytes);
 b2g_status b2g_stack_workspace_init(const b2g_stack* st, void* workspace, b2g_stream_t stream);
+/* Execution mode (key B2G_STACK_OPT_MODE):
+ *  PERSISTENT (default): one cooperative launch runs every layer (up to 32
+ *    layers per launch), grid barriers between the gate||up and down phases;
+ *    each phase's first weights are loaded while the barrier completes.
+ *  PER_LAYER: two launches per layer chained with programmatic dependent
+ *    launch and an L2 prefetch of the next launch's first weights.
+ * Both give bitwise-identical results. */
+enum { B2G_STACK_OPT_MODE = 1 };
+enum { B2G_STACK_MODE_PERSISTENT = 0, B2G_STACK_MODE_PER_LAYER = 1 };
+b2g_status b2g_stack_set_option(b2g_stack* st, int32_t key, int32_t value);
 /* h [m, hidden] fp16 is read and overwritten; act is [m, intermediate] fp16
- * scratch.  Launches 2 kernels per layer chained with programmatic dependent
- * launch.  tp_size > 1 is not handled here (see the Python TP driver). */
+ * scratch.  The workspace must have been zeroed once by
+ * b2g_stack_workspace_init (and again after a call that reported a device
+ * error).  tp_size > 1 is not handled here (see the Python TP driver). */
 b2g_status b2g_stack_enqueue(const b2g_stack* st, int32_t m, void* h, void* act,
                              void* workspace, b2g_stream_t stream);
 

@@ -27,6 +27,8 @@ LAYOUT = {"KN": 0, "NK": 1}
 FUSE_NONE, FUSE_GATE_UP_SILU, FUSE_RMSNORM_INPUT, FUSE_RESIDUAL_ADD = 0, 1, 2, 4
 OPT_MATH, OPT_GRID = 1, 2
 MATH_MMA, MATH_FFMA = 0, 1
+STACK_OPT_MODE = 1
+STACK_MODE_PERSISTENT, STACK_MODE_PER_LAYER = 0, 1
 
 
 class B2GError(RuntimeError):
@@ -90,6 +92,7 @@ SIGNATURES = {
     "b2g_stack_create": ([ctypes.POINTER(StackFields), ctypes.POINTER(_P)], ctypes.c_int),
     "b2g_stack_destroy": ([_P], ctypes.c_int),
     "b2g_stack_ops": ([_P, ctypes.POINTER(_P), ctypes.POINTER(_P)], ctypes.c_int),
+    "b2g_stack_set_option": ([_P, _I32, _I32], ctypes.c_int),
     "b2g_stack_set_layer": ([_P, _I32, _P, _P, _P, _P], ctypes.c_int),
     "b2g_stack_workspace_size": ([_P, _I32, ctypes.POINTER(_SZ)], ctypes.c_int),
     "b2g_stack_workspace_init": ([_P, _P, _P], ctypes.c_int),
@@ -291,6 +294,12 @@ class Stack:
         if getattr(self, "h", None) and _lib is not None:
             _lib.b2g_stack_destroy(self.h)
             self.h = None
+
+    def set_mode(self, mode):
+        """STACK_MODE_PERSISTENT (one cooperative launch) or STACK_MODE_PER_LAYER."""
+        check(lib().b2g_stack_set_option(self.h, STACK_OPT_MODE, _code(
+            {"persistent": STACK_MODE_PERSISTENT, "per_layer": STACK_MODE_PER_LAYER}, mode)),
+            "b2g_stack_set_option")
 
     def set_layer(self, layer, packed_gu, scales_gu, packed_d, scales_d):
         self._keep[layer] = (packed_gu, scales_gu, packed_d, scales_d)

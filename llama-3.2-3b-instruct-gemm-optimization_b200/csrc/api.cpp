@@ -36,6 +36,7 @@ struct b2g_stack {
   b2g_stack_fields f;
   b2g_op* gu;
   b2g_op* dn;
+  int mode;  // B2G_STACK_MODE_*
   struct Layer {
     const void *pgu, *sgu, *pd, *sd;
   };
@@ -122,6 +123,31 @@ b2g_status replan(b2g_op* op) {
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// The plan-derived fields of one GEMV launch over `workspace` for m rows.
+void fill_plan(const b2g_op* op, int m, const LaunchPlan& lp, void* workspace, int dev, GemvParams* p) {
+  p->counters = static_cast<int*>(workspace);
+  p->partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterRegionBytes);
+  p->error = g_err_word[dev];
+  p->total_units = op->total_units;
+  p->r_units = 1.0 / (double)op->total_units;
+  p->r_grid = 1.0 / (double)op->grid;
+  p->grid = op->grid;
+  p->n_tiles = op->n_tiles;
+  p->kb_total = op->kb_total;
+  p->ksplit = op->ksplit;
+  p->kbpv = op->kbpv;
+  p->M = m;
+  p->K = op->K;
+  p->N = op->N;
+  p->scale_mode = op->f.scale_mode;
+  p->rmsnorm = (op->f.fuse & B2G_FUSE_RMSNORM_INPUT) ? 1 : 0;
+  p->residual_add = (op->f.fuse & B2G_FUSE_RESIDUAL_ADD) ? 1 : 0;
+  p->max_contrib = op->max_contrib;
+  p->n_slots = op->n_slots;
+  p->off_x = lp.off_x;
+  p->x_rs = lp.x_rs;
+}
 
 }  // namespace
 
@@ -326,6 +352,7 @@ b2g_status b2g_enqueue_ex(const b2g_op* op, const b2g_enqueue_args* a, b2g_strea
   if (!plan_launch(op, a->m, &lp)) return B2G_ERR_OOM;
 
   GemvParams p = {};
+  fill_plan(op, a->m, lp, a->workspace, dev, &p);
   p.packed = static_cast<const uint8_t*>(a->packed_w);
   p.x = static_cast<const __half*>(a->x);
   p.ldx = a->ldx;
@@ -334,27 +361,7 @@ b2g_status b2g_enqueue_ex(const b2g_op* op, const b2g_enqueue_args* a, b2g_strea
   p.ldr = a->ldr;
   p.y = static_cast<__half*>(a->y);
   p.ldy = a->ldy;
-  p.counters = static_cast<int*>(a->workspace);
-  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(a->workspace) + kCounterRegionBytes);
-  p.error = g_err_word[dev];
-  p.total_units = op->total_units;
-  p.grid = op->grid;
-  p.n_tiles = op->n_tiles;
-  p.kb_total = op->kb_total;
-  p.ksplit = op->ksplit;
-  p.kbpv = op->kbpv;
-  p.M = a->m;
-  p.K = op->K;
-  p.N = op->N;
-  p.scale_mode = op->f.scale_mode;
-  p.rmsnorm = (op->f.fuse & B2G_FUSE_RMSNORM_INPUT) ? 1 : 0;
-  p.residual_add = resid ? 1 : 0;
   p.rms_eps = a->rms_eps;
-  p.max_contrib = op->max_contrib;
-  p.n_slots = op->n_slots;
-  p.off_x = lp.off_x;
-  p.x_rs = lp.x_rs;
-  p.x_tma = (aligned(a->x, 16) && (a->ldx % 8) == 0 && (op->K % 32) == 0) ? 1 : 0;
   if (a->prefetch_op && a->prefetch_packed) {
     const b2g_op* nx = a->prefetch_op;
     if (!aligned(a->prefetch_packed, 16)) return B2G_ERR_INVALID;
@@ -362,7 +369,7 @@ b2g_status b2g_enqueue_ex(const b2g_op* op, const b2g_enqueue_args* a, b2g_strea
     p.pf_total_units = nx->total_units;
     p.pf_unit_bytes = nx->unit_bytes;
     p.pf_grid = nx->grid;
-    p.pf_bytes = 131072;  // one CTA's initial loads (128 KB in flight per SM)
+    p.pf_bytes = 1 << 30;  // the CTA's whole range
   }
   return cuda_status(launch_gemv(p, op->planes, op->wbytes, op->math, lp.smem, a->pdl != 0,
                                  reinterpret_cast<cudaStream_t>(stream)));
@@ -519,8 +526,69 @@ b2g_status b2g_stack_workspace_init(const b2g_stack* st, void* ws, b2g_stream_t 
   return cuda_status(cudaMemsetAsync(ws, 0, bytes, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+b2g_status b2g_stack_set_option(b2g_stack* st, int32_t key, int32_t value) {
+  if (!st) return B2G_ERR_INVALID;
+  if (key != B2G_STACK_OPT_MODE) return B2G_ERR_INVALID;
+  if (value != B2G_STACK_MODE_PERSISTENT && value != B2G_STACK_MODE_PER_LAYER) return B2G_ERR_INVALID;
+  st->mode = value;
+  return B2G_OK;
+}
+
+// All layers in cooperative launches of up to kMaxStackLayers layers each.
+static b2g_status stack_enqueue_persistent(const b2g_stack* st, int32_t m, void* h, void* act, void* ws,
+                                           cudaStream_t stream) {
+  const b2g_op* gu = st->gu;
+  const b2g_op* dn = st->dn;
+  if (gu->grid != dn->grid || gu->wbytes != dn->wbytes) return B2G_ERR_UNSUPPORTED;
+  if (!aligned(ws, 16) || !aligned(h, 2) || !aligned(act, 2)) return B2G_ERR_INVALID;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B2G_ERR_CUDA;
+  if (dev != gu->device) return B2G_ERR_INVALID;
+  b2g_status s = ensure_device_setup(dev, gu->smem_optin);
+  if (s != B2G_OK) return s;
+  LaunchPlan lg, ld;
+  if (!plan_launch(gu, m, &lg) || !plan_launch(dn, m, &ld)) return B2G_ERR_OOM;
+  const size_t smem = std::max(lg.smem, ld.smem);
+  int max_grid = 0;
+  if (stack_max_coresident(gu->wbytes, smem, gu->num_sms, &max_grid) != cudaSuccess) return B2G_ERR_CUDA;
+  if (gu->grid > max_grid) return B2G_ERR_UNSUPPORTED;
+  StackParams sp = {};
+  fill_plan(gu, m, lg, ws, dev, &sp.gu);
+  fill_plan(dn, m, ld, ws, dev, &sp.dn);
+  sp.gu.rms_eps = st->f.rms_eps;
+  sp.h = static_cast<__half*>(h);
+  sp.ldh = st->f.hidden;
+  sp.act = static_cast<__half*>(act);
+  sp.ldact = st->f.intermediate;
+  sp.barrier = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + kBarrierWordOffset);
+  for (int l0 = 0; l0 < st->f.n_layers; l0 += kMaxStackLayers) {
+    sp.n_layers = std::min(kMaxStackLayers, st->f.n_layers - l0);
+    for (int i = 0; i < sp.n_layers; ++i) {
+      const auto& L = st->layers[l0 + i];
+      sp.layers[i] = StackLayer{static_cast<const uint8_t*>(L.pgu), L.sgu, static_cast<const uint8_t*>(L.pd),
+                                L.sd};
+    }
+    if (launch_stack(sp, gu->wbytes, smem, stream) != cudaSuccess) return B2G_ERR_CUDA;
+  }
+  return B2G_OK;
+}
+
 b2g_status b2g_stack_enqueue(const b2g_stack* st, int32_t m, void* h, void* act, void* ws, b2g_stream_t stream) {
   if (!st || !h || !act || !ws) return B2G_ERR_INVALID;
+  if (m < 1 || m > st->f.max_m) return B2G_ERR_INVALID;
+  for (int l = 0; l < st->f.n_layers; ++l) {
+    const auto& L = st->layers[l];
+    if (!L.pgu || !L.pd) return B2G_ERR_INVALID;
+    if (!aligned(L.pgu, 16) || !aligned(L.pd, 16)) return B2G_ERR_INVALID;
+    if (st->f.scale_mode == B2G_SCALE_CHANNEL_FP32 && (!aligned(L.sgu, 4) || !aligned(L.sd, 4)))
+      return B2G_ERR_INVALID;
+  }
+  if (st->mode == B2G_STACK_MODE_PERSISTENT) {
+    // Shapes whose two phases plan different grids, or a grid that cannot be
+    // co-resident, run per layer instead.
+    const b2g_status s = stack_enqueue_persistent(st, m, h, act, ws, reinterpret_cast<cudaStream_t>(stream));
+    if (s != B2G_ERR_UNSUPPORTED) return s;
+  }
   for (int l = 0; l < st->f.n_layers; ++l) {
     const auto& L = st->layers[l];
     if (!L.pgu || !L.pd) return B2G_ERR_INVALID;

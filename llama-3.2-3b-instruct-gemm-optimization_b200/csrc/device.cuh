@@ -14,6 +14,7 @@ enum : int {
   kErrEmptyWait = 2,  // the producer waited too long for consumers
   kErrDrainWait = 3,  // an in-flight copy did not land while aborting
   kErrPeerWait = 4,   // a wait on another GPU's flag expired
+  kErrGridWait = 5,   // a grid-wide barrier of the stack kernel expired
 };
 
 // A wait gives up after this many nanoseconds of %globaltimer.  Long enough
@@ -156,6 +157,26 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t v16) {
   return r;
 }
 
+// Four E4M3 codes (byte i = element i) -> two f16x2 (elements 0,1 and 2,3).
+// The 32-bit word is split into its 16-bit halves in registers (no shift).
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 a, b;\n\t"
+      "mov.b32 {a, b}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, a;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
+
+// Atomic add at GPU scope with acquire-release semantics: publishes this
+// thread's earlier writes (and those ordered before it) and, for the thread
+// that observes the final count, makes the other publishers' writes visible.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // float -> E4M3 code, round to nearest even, saturate to +-448.
 __device__ __forceinline__ uint8_t f32_to_e4m3(float f) {
   uint16_t r;
@@ -189,6 +210,19 @@ __device__ __forceinline__ uint4 lds128(const void* p) {
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "r"(smem_addr(p)));
+  return v;
+}
+
+// Loads at a 32-bit shared-memory address.
+__device__ __forceinline__ uint4 lds128_at(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+
+__device__ __forceinline__ uint2 lds64_at(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
   return v;
 }
 

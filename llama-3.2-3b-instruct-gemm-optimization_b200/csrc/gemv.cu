@@ -1,4 +1,4 @@
-// gemv.cu -- stream-K decode GEMV for sm_100a.
+// gemv.cu -- stream-K decode GEMV and the persistent decode-MLP stack for sm_100a.
 //
 // y[m, n] = epilogue( s[n] * sum_k x[m, k] * W[k, n] ),  m < M <= 8.
 //
@@ -12,15 +12,17 @@
 //  * Weights go straight from HBM into registers: each lane's 16 B of a unit
 //    (16 output channels x 32 k for E4M3, x 16 k for FP16) is exactly its
 //    m16n8k16 A fragment, loaded with ld.global.nc.L1::no_allocate (L2
-//    evict-first) 8-16 units ahead, 128 KB in flight per SM.  The first loads
-//    are issued before waiting on the previous kernel (weights are
-//    constant), and the tail of the stream warms L2 for the next kernel.
-//  * The M <= 8 activation rows are staged once per CTA in shared memory by
-//    bulk copy (RMSNorm applied there when fused), with the k order inside each
-//    32-block permuted by the prepack so a lane's B fragment is one 16 B load;
-//    the decode rows fill the n = 8 side of mma.sync.m16n8k16 (x^T as B).
-//  * E4M3 is widened to f16 in registers (cvt.rn.f16x2.e4m3x2).  A CUDA-core
-//    FFMA variant of the same loop (kMathFfma) exists for comparison.
+//    evict-first) 16 (one plane) or 8 (two planes) units ahead: 128 KB in
+//    flight per SM.  A phase's first loads are issued before its activations
+//    exist (before the previous kernel is waited on, or before the stack
+//    kernel's grid barrier), since weights are constant.
+//  * The M <= 8 activation rows are staged once per phase in shared memory
+//    with one round of 16 B loads (RMSNorm applied there when fused).  The
+//    prepack permutes k inside each block so a lane's B fragment is one 16 B
+//    (E4M3) or 8 B (FP16) shared load; the decode rows fill the n = 8 side of
+//    mma.sync.m16n8k16 (x^T as B).  E4M3 is widened with cvt.rn.f16x2.e4m3x2.
+//    A CUDA-core FFMA variant of the same loop (kMathFfma) exists for
+//    comparison.
 //  * Each warp's partial per virtual tile goes to a shared-memory slot.  After
 //    the stream the slots are summed in warp order, and a tile split across
 //    CTAs is summed in (k-range, CTA) order by the last CTA to arrive (one
@@ -29,6 +31,10 @@
 //    memset, no separate cast kernel.
 //  * Epilogues: per-channel/tensor scale, fp16 rounding, SiLU(gate)*up for the
 //    fused gate||up op, residual add.
+//  * stack_kernel runs the layers of the decode MLP in one cooperative launch:
+//    phases [RMSNorm + gate||up + SiLU*up] and [down + residual] per layer,
+//    separated by bounded grid barriers, each phase's first weights already in
+//    flight while the barrier and the activation staging complete.
 #include <cstdio>
 #include <type_traits>
 
@@ -40,11 +46,17 @@ namespace b2g {
 __device__ int g_device_error;
 
 #ifdef B2G_TRACE
-// Per-CTA phase timestamps (%globaltimer), debug builds only.
+// Per-CTA phase timestamps (%globaltimer), debug builds only.  g_trace: the
+// single-op kernel's points; g_strace: 4 points per stack phase.
+constexpr int kTracePts = 256;
 __device__ unsigned long long g_trace[1024][16];
+__device__ unsigned long long g_strace[160][kTracePts];
 #define TRACE(i) do { g_trace[blockIdx.x][(i)] = globaltimer_ns(); } while (0)
+#define STRACE(i) \
+  do { if ((i) >= 0 && (i) < kTracePts && blockIdx.x < 160) g_strace[blockIdx.x][(i)] = globaltimer_ns(); } while (0)
 #else
 #define TRACE(i) do { } while (0)
+#define STRACE(i) do { } while (0)
 #endif
 
 int* device_error_word() {
@@ -57,19 +69,55 @@ namespace {
 
 constexpr int W = kWarps;
 constexpr int NT = kThreads;
+constexpr int kRing = 16;  // uint4 registers per lane for in-flight weight units
 
-__device__ __forceinline__ long long cta_of(long long u, long long T, int G) {
-  return ((u + 1) * G + T - 1) / T - 1;
+// The buffers one GEMV phase reads and writes.
+struct Io {
+  const uint8_t* packed;
+  const void* scales;
+  const __half* x;
+  long long ldx;
+  const __half* residual;
+  long long ldr;
+  __half* y;
+  long long ldy;
+};
+
+__device__ __forceinline__ Io io_of_params(const GemvParams& p) {
+  return Io{p.packed, p.scales, p.x, p.ldx, p.residual, p.ldr, p.y, p.ldy};
 }
 
-__device__ __forceinline__ float channel_scale(const GemvParams& p, int plane, int n) {
+// floor(a / b) for 0 <= a < 2^52 and 0 < b < 2^31, given rb = 1.0 / b
+// rounded to nearest: the double product is within one of the quotient, and
+// one integer correction makes it exact.  (A 64-bit integer division is a
+// long dependent instruction sequence; this is a handful of instructions.)
+__device__ __forceinline__ long long floor_div(long long a, long long b, double rb) {
+  long long q = (long long)((double)a * rb);
+  if (q * b > a)
+    --q;
+  else if ((q + 1) * b <= a)
+    ++q;
+  return q;
+}
+
+// The CTA whose stream-K range [c*T/G, (c+1)*T/G) holds unit u.
+__device__ __forceinline__ int cta_of(const GemvParams& p, long long u) {
+  return (int)floor_div((u + 1) * p.grid + p.total_units - 1, p.total_units, p.r_units) - 1;
+}
+
+// First unit of CTA c's range.
+__device__ __forceinline__ int range_start(const GemvParams& p, int c) {
+  return (int)floor_div((long long)c * p.total_units, p.grid, p.r_grid);
+}
+
+__device__ __forceinline__ float channel_scale(const GemvParams& p, const Io& io, int plane, int n) {
   switch (p.scale_mode) {
     case 1:
-      return __half2float(reinterpret_cast<const __half*>(p.scales)[plane]);
+      return __half2float(reinterpret_cast<const __half*>(io.scales)[plane]);
     case 2:
-      return __half2float(reinterpret_cast<const __half*>(p.scales)[(size_t)plane * p.N + n]);
+      return __half2float(reinterpret_cast<const __half*>(io.scales)[(size_t)plane * p.N + n]);
     case 3:
-      return reinterpret_cast<const float*>(p.scales)[(size_t)plane * p.N + n];
+      return reinterpret_cast<const float*>(io.scales)[(size_t)plane * p.N + n];
     default:
       return 1.0f;
   }
@@ -89,7 +137,7 @@ __device__ __forceinline__ uint32_t f2_to_h2(float a, float b) {
 // Lane layout of a finished tile (the m16n8 accumulator): entry i of lane
 // (g = lane/4, q = lane%4) is channel g + 8*(i/2), token 2q + (i%2).
 template <int P>
-__device__ void epilogue(const GemvParams& p, int tile, const float (&v)[P][4], int lane) {
+__device__ void epilogue(const GemvParams& p, const Io& io, int tile, const float (&v)[P][4], int lane) {
   const int g = lane >> 2, q = lane & 3;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -98,117 +146,123 @@ __device__ void epilogue(const GemvParams& p, int tile, const float (&v)[P][4], 
     if (m < p.M && n < p.N) {
       __half out;
       if constexpr (P == 1) {
-        out = __float2half_rn(v[0][i] * channel_scale(p, 0, n));
+        out = __float2half_rn(v[0][i] * channel_scale(p, io, 0, n));
         if (p.residual_add)
-          out = __float2half_rn(__half2float(__ldcg(p.residual + (size_t)m * p.ldr + n)) +
+          out = __float2half_rn(__half2float(__ldcg(io.residual + (size_t)m * io.ldr + n)) +
                                 __half2float(out));
       } else {
-        const float gf = __half2float(__float2half_rn(v[0][i] * channel_scale(p, 0, n)));
-        const float uf = __half2float(__float2half_rn(v[1][i] * channel_scale(p, 1, n)));
+        const float gf = __half2float(__float2half_rn(v[0][i] * channel_scale(p, io, 0, n)));
+        const float uf = __half2float(__float2half_rn(v[1][i] * channel_scale(p, io, 1, n)));
         out = __float2half_rn(gf / (1.0f + expf(-gf)) * uf);
       }
-      p.y[(size_t)m * p.ldy + n] = out;
+      io.y[(size_t)m * io.ldy + n] = out;
     }
   }
-}
-
-// Address of the idx-th partial of output tile `tile`, contributions ordered
-// by (k-range, CTA).
-template <int P>
-__device__ __forceinline__ const float4* contrib_ptr(const GemvParams& p, int tile, int idx) {
-  const long long T = p.total_units;
-  for (int k = 0; k < p.ksplit; ++k) {
-    const long long vt = (long long)k * p.n_tiles + tile;
-    const long long a = vt * p.kbpv;
-    const int n = (int)(cta_of(a + p.kbpv - 1, T, p.grid) - cta_of(a, T, p.grid)) + 1;
-    if (idx < n)
-      return reinterpret_cast<const float4*>(p.partials) + ((size_t)vt * p.max_contrib + idx) * P * 32;
-    idx -= n;
-  }
-  return nullptr;
 }
 
 // A virtual tile's CTA-level sum is complete in v: finish it here if this CTA
 // is the tile's only contributor, else publish it and let the last
 // contributing CTA sum all partials in (k-range, CTA) order.
+constexpr int kMaxKsplit = 8;
 template <int P>
-__device__ void finish_vt(const GemvParams& p, long long vt, const float (&v)[P][4], int lane) {
-  const long long T = p.total_units;
-  const int G = p.grid;
-  const int ks = (int)(vt / p.n_tiles);
-  const int tile = (int)(vt - (long long)ks * p.n_tiles);
-  int total = 0;
-  for (int k = 0; k < p.ksplit; ++k) {
-    const long long a = ((long long)k * p.n_tiles + tile) * p.kbpv;
-    total += (int)(cta_of(a + p.kbpv - 1, T, G) - cta_of(a, T, G)) + 1;
+__device__ __forceinline__ void finish_vt(const GemvParams& p, const Io& io, int vt, const float (&v)[P][4],
+                                          int lane) {
+  // k-ranges whose partials are fetched in one round trip (the rest, and
+  // contributors past the second of a k-range, are read one at a time).
+  constexpr int KU = (P == 1) ? 4 : 2;
+  const int ks = vt / p.n_tiles;
+  const int tile = vt - ks * p.n_tiles;
+  int cf[kMaxKsplit], cn[kMaxKsplit];  // first contributing CTA and count per k-range
+  int total = 0, my_first = 0;
+#pragma unroll
+  for (int k = 0; k < kMaxKsplit; ++k) {
+    cf[k] = 0;
+    cn[k] = 0;
+    if (k < p.ksplit) {
+      const long long a = (long long)(k * p.n_tiles + tile) * p.kbpv;
+      cf[k] = cta_of(p, a);
+      cn[k] = cta_of(p, a + p.kbpv - 1) - cf[k] + 1;
+      total += cn[k];
+      if (k == ks) my_first = cf[k];
+    }
   }
   if (total == 1) {
-    epilogue<P>(p, tile, v, lane);
+    epilogue<P>(p, io, tile, v, lane);
     return;
   }
-  const long long c_first = cta_of(vt * p.kbpv, T, G);
-  float4* dst = reinterpret_cast<float4*>(p.partials) +
-                ((size_t)vt * p.max_contrib + (size_t)(blockIdx.x - c_first)) * P * 32;
+  float4* parts = reinterpret_cast<float4*>(p.partials);
+  float4* dst = parts + ((size_t)vt * p.max_contrib + (size_t)(blockIdx.x - my_first)) * P * 32;
 #pragma unroll
   for (int pl = 0; pl < P; ++pl)
     __stcg(&dst[pl * 32 + lane], make_float4(v[pl][0], v[pl][1], v[pl][2], v[pl][3]));
-  fence_acq_rel_gpu();
   __syncwarp();
   int old = 0;
-  if (lane == 0) old = atomicAdd(&p.counters[tile], 1);
+  if (lane == 0) old = atom_add_acq_rel_gpu(&p.counters[tile], 1);
   old = __shfl_sync(0xffffffffu, old, 0);
   if (old != total - 1) return;
   fence_acq_rel_gpu();
+  auto src = [&](int k, int c) {
+    return parts + ((size_t)(k * p.n_tiles + tile) * p.max_contrib + c) * P * 32 + lane;
+  };
+  float4 t[KU][2][P];
+#pragma unroll
+  for (int k = 0; k < KU; ++k)
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+      for (int pl = 0; pl < P; ++pl)
+        t[k][c][pl] = (k < p.ksplit && c < cn[k]) ? __ldcg(src(k, c) + pl * 32) : make_float4(0.f, 0.f, 0.f, 0.f);
   float s[P][4];
 #pragma unroll
   for (int pl = 0; pl < P; ++pl) s[pl][0] = s[pl][1] = s[pl][2] = s[pl][3] = 0.f;
-  constexpr int B = 4;  // partials fetched per round trip
-  for (int base = 0; base < total; base += B) {
-    float4 t[B][P];
+  auto add = [&](int pl, const float4& a) {
+    s[pl][0] += a.x;
+    s[pl][1] += a.y;
+    s[pl][2] += a.z;
+    s[pl][3] += a.w;
+  };
 #pragma unroll
-    for (int b = 0; b < B; ++b) {
-      if (base + b < total) {
-        const float4* src = contrib_ptr<P>(p, tile, base + b);
+  for (int k = 0; k < kMaxKsplit; ++k) {
+    if (k >= p.ksplit) break;
+    int c = 0;
+    if (k < KU) {
 #pragma unroll
-        for (int pl = 0; pl < P; ++pl) t[b][pl] = __ldcg(&src[pl * 32 + lane]);
+      for (int pl = 0; pl < P; ++pl) {
+        if (cn[k] > 0) add(pl, t[k < KU ? k : 0][0][pl]);
+        if (cn[k] > 1) add(pl, t[k < KU ? k : 0][1][pl]);
       }
+      c = 2;
     }
+    for (; c < cn[k]; ++c) {
 #pragma unroll
-    for (int b = 0; b < B; ++b) {
-      if (base + b < total) {
-#pragma unroll
-        for (int pl = 0; pl < P; ++pl) {
-          s[pl][0] += t[b][pl].x;
-          s[pl][1] += t[b][pl].y;
-          s[pl][2] += t[b][pl].z;
-          s[pl][3] += t[b][pl].w;
-        }
-      }
+      for (int pl = 0; pl < P; ++pl) add(pl, __ldcg(src(k, c) + pl * 32));
     }
   }
   if (lane == 0) p.counters[tile] = 0;
-  epilogue<P>(p, tile, s, lane);
+  epilogue<P>(p, io, tile, s, lane);
 }
 
 // ---------------------------------------------------------------------------
 // Activation rows in shared memory: row m at xs + m * x_rs (halves), holding
-// k in [k_lo, k_lo + krange).  The row stride is = 8 (mod 64) halves so the
-// eight rows of a B fragment fall in different banks.
+// k in [k_lo, k_lo + krange), zero beyond K.  All threads load 16 B pieces,
+// up to 8 each in flight (M = 8 rows of 3072 halves is one round).  L2 loads
+// (ld.cg): x may have been written by another CTA of the same launch.
 // ---------------------------------------------------------------------------
-__device__ void stage_x_manual(const GemvParams& p, __half* xs, int k_lo, int krange, int tid) {
+__device__ void stage_x(const GemvParams& p, const Io& io, __half* xs, int k_lo, int krange, int tid) {
   const int M = p.M, K = p.K;
-  const bool vec = ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0) && ((p.ldx & 7) == 0);
+  const bool vec = ((reinterpret_cast<uintptr_t>(io.x) & 15) == 0) && ((io.ldx & 7) == 0);
   const int nch = krange / 8;
-  for (int idx = tid; idx < M * nch; idx += NT * 4) {
-    uint4 v[4];
+  const int total = M * nch;
+  for (int idx = tid; idx < total; idx += NT * 8) {
+    uint4 v[8];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+    for (int r = 0; r < 8; ++r) {
       const int id = idx + r * NT;
       v[r] = make_uint4(0, 0, 0, 0);
-      if (id < M * nch) {
+      if (id < total) {
         const int m = id / nch, c = id - m * nch;
         const int k0 = k_lo + c * 8;
-        const __half* row = p.x + (size_t)m * p.ldx;
+        const __half* row = io.x + (size_t)m * io.ldx;
         if (vec && k0 + 8 <= K) {
           v[r] = __ldcg(reinterpret_cast<const uint4*>(row + k0));
         } else {
@@ -221,9 +275,9 @@ __device__ void stage_x_manual(const GemvParams& p, __half* xs, int k_lo, int kr
       }
     }
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+    for (int r = 0; r < 8; ++r) {
       const int id = idx + r * NT;
-      if (id < M * nch) {
+      if (id < total) {
         const int m = id / nch, c = id - m * nch;
         sts128(xs + (size_t)m * p.x_rs + c * 8, v[r]);
       }
@@ -249,13 +303,13 @@ __device__ void rmsnorm_rows(const GemvParams& p, __half* xs, float* rms_r, floa
     for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
     if ((tid & 31) == 0) red[(tid >> 5) * 8 + m] = s;
   }
-  named_sync(1, NT);
+  __syncthreads();
   if (tid < M) {
     float t = 0.f;
     for (int w = 0; w < W; ++w) t += red[w * 8 + tid];
     rms_r[tid] = 1.0f / sqrtf(t / (float)K + p.rms_eps);
   }
-  named_sync(1, NT);
+  __syncthreads();
   for (int idx = tid; idx < M * nch; idx += NT) {
     const int m = idx / nch, c = idx - m * nch;
     __half* at = xs + (size_t)m * p.x_rs + c * 8;
@@ -268,7 +322,7 @@ __device__ void rmsnorm_rows(const GemvParams& p, __half* xs, float* rms_r, floa
 }
 
 // ---------------------------------------------------------------------------
-// Per-unit math.  `xk` points at the unit's first k in row 0 of the staged x.
+// Per-unit math
 // ---------------------------------------------------------------------------
 template <int P, int WB>
 struct MmaMath {
@@ -277,22 +331,22 @@ struct MmaMath {
 #pragma unroll
     for (int pl = 0; pl < P; ++pl) acc[pl][0] = acc[pl][1] = acc[pl][2] = acc[pl][3] = 0.f;
   }
-  // xf: this lane's B fragment for the unit (b0..b3 for E4M3; b0, b1 for FP16).
-  __device__ __forceinline__ void unit(const uint4 (&wv)[P], const uint4& xf) {
-    if constexpr (WB == 1) {
+  // w: this lane's A fragments (one uint4 per plane); xf: its B fragment
+  // (b0..b3 for E4M3, two k16 steps; b0, b1 for FP16).
+  __device__ __forceinline__ void unit(const uint4* w, const uint4& xf) {
 #pragma unroll
-      for (int pl = 0; pl < P; ++pl) {
-        const uint4 w = wv[pl];
-        mma_16816(acc[pl], e4m3x2_to_f16x2(w.x), e4m3x2_to_f16x2(w.x >> 16), e4m3x2_to_f16x2(w.y),
-                  e4m3x2_to_f16x2(w.y >> 16), xf.x, xf.y);
-        mma_16816(acc[pl], e4m3x2_to_f16x2(w.z), e4m3x2_to_f16x2(w.z >> 16), e4m3x2_to_f16x2(w.w),
-                  e4m3x2_to_f16x2(w.w >> 16), xf.z, xf.w);
-      }
-    } else {
-#pragma unroll
-      for (int pl = 0; pl < P; ++pl) {
-        const uint4 w = wv[pl];
-        mma_16816(acc[pl], w.x, w.y, w.z, w.w, xf.x, xf.y);
+    for (int pl = 0; pl < P; ++pl) {
+      const uint4 a = w[pl];
+      if constexpr (WB == 1) {
+        uint32_t h0, h1, h2, h3;
+        e4m3x4_to_f16x2x2(a.x, h0, h1);
+        e4m3x4_to_f16x2x2(a.y, h2, h3);
+        mma_16816(acc[pl], h0, h1, h2, h3, xf.x, xf.y);
+        e4m3x4_to_f16x2x2(a.z, h0, h1);
+        e4m3x4_to_f16x2x2(a.w, h2, h3);
+        mma_16816(acc[pl], h0, h1, h2, h3, xf.z, xf.w);
+      } else {
+        mma_16816(acc[pl], a.x, a.y, a.z, a.w, xf.x, xf.y);
       }
     }
   }
@@ -316,14 +370,14 @@ struct FfmaMath {
         for (int m = 0; m < 8; ++m) acc[pl][c][m] = 0.f;
   }
   // xk: this lane's x slice of the unit in row 0 (row m at xk + m * rs).
-  __device__ __forceinline__ void unit(const uint4 (&wv)[P], const __half* xk, int M, int rs) {
+  __device__ __forceinline__ void unit(const uint4* w, const __half* xk, int M, int rs) {
     constexpr int S = (WB == 1) ? 2 : 1;  // k16 steps per unit
     float2 wf[P][S][4];                   // [plane][step][register r]
 #pragma unroll
     for (int pl = 0; pl < P; ++pl) {
-      const uint4 w = wv[pl];
+      const uint4 a = w[pl];
       if constexpr (WB == 1) {
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        const uint32_t ws[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
         for (int s = 0; s < 2; ++s)
 #pragma unroll
@@ -332,10 +386,10 @@ struct FfmaMath {
             wf[pl][s][r] = h2_to_f2(e4m3x2_to_f16x2((r & 1) ? (word >> 16) : word));
           }
       } else {
-        wf[pl][0][0] = h2_to_f2(w.x);
-        wf[pl][0][1] = h2_to_f2(w.y);
-        wf[pl][0][2] = h2_to_f2(w.z);
-        wf[pl][0][3] = h2_to_f2(w.w);
+        wf[pl][0][0] = h2_to_f2(a.x);
+        wf[pl][0][1] = h2_to_f2(a.y);
+        wf[pl][0][2] = h2_to_f2(a.z);
+        wf[pl][0][3] = h2_to_f2(a.w);
       }
     }
 #pragma unroll
@@ -395,109 +449,118 @@ struct FfmaMath {
 };
 
 // ---------------------------------------------------------------------------
-// The kernel
+// Phase pieces.  A phase is one GEMV over this CTA's range of the stream.
+// The ring holds R uint4 per lane: unit d of the warp's next D = R / P units
+// in ring[d*P .. d*P + P - 1].
 // ---------------------------------------------------------------------------
-template <int P, int WB, int MATH>
-__global__ void __launch_bounds__(kThreads, 1)
-    gemv_streamk_kernel(const __grid_constant__ GemvParams p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+struct Range {
+  int u0, u1, n_mine;  // CTA's units [u0, u1); this warp's count (units u0 + warp + j*W)
+};
+
+__device__ __forceinline__ Range cta_range(const GemvParams& p, int warp) {
+  Range r;
+  r.u0 = range_start(p, blockIdx.x);
+  r.u1 = range_start(p, blockIdx.x + 1);
+  const int n = r.u1 - r.u0;
+  r.n_mine = n > warp ? (n - warp + W - 1) / W : 0;
+  return r;
+}
+
+// Issue the loads of this warp's first D units of a phase.  Every ring entry
+// is written (zero past the warp's units), so the compiler sees the old
+// contents die here and does not keep them live across a phase's combine.
+template <int P, int R>
+__device__ __forceinline__ void prefetch_phase(const GemvParams& p, const uint8_t* packed,
+                                               uint4 (&ring)[R], int warp, int lane, uint64_t pol) {
+  constexpr int D = R / P;
   constexpr int UNIT = P * kUnitPlaneBytes;
-  // Units each lane keeps in flight: 16 B x 512 threads x D x P = 128 KB per SM.
-  constexpr int D = (MATH == kMathMma) ? (P == 1 ? 16 : 8) : (P == 1 ? 8 : 4);
+  constexpr size_t WSTEP = (size_t)W * UNIT;
+  const Range r = cta_range(p, warp);
+  const uint8_t* wl = packed + ((size_t)r.u0 + warp) * UNIT + lane * 16;
+#pragma unroll
+  for (int d = 0; d < D; ++d) {
+#pragma unroll
+    for (int pl = 0; pl < P; ++pl)
+      ring[d * P + pl] = d < r.n_mine ? ldg_stream(wl + d * WSTEP + pl * kUnitPlaneBytes, pol)
+                                      : make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Warm L2 with the first `bytes` of this CTA's range of a phase (one thread
+// issues bulk prefetches; no registers, no completion to wait for).
+__device__ __forceinline__ void l2_prefetch_phase(const GemvParams& p, const uint8_t* packed, int unit_bytes,
+                                                  long long bytes) {
+  if (threadIdx.x != 0) return;
+  const long long a = range_start(p, blockIdx.x);
+  const long long b = range_start(p, blockIdx.x + 1);
+  bytes = min(bytes, (b - a) * unit_bytes);
+  const uint8_t* src = packed + a * unit_bytes;
+  for (long long off = 0; off < bytes; off += 32768)
+    bulk_prefetch_l2(src + off, (uint32_t)min(32768LL, bytes - off));
+}
+
+// One phase with the ring pre-filled by prefetch_phase: stage x (and
+// RMSNorm it), stream the rest of the range, leave each warp's partial per
+// virtual tile in a shared slot, run after_stream(ring) (the ring is idle
+// then: e.g. prefetch the next phase), then combine and finish the tiles.
+// Entry requires every thread of the CTA to be past its last read of the
+// shared slots and x rows of any earlier phase.
+template <int P, int WB, int MATH, int R, class AfterStream>
+__device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uint8_t* smem,
+                                          uint4 (&ring)[R], uint64_t pol, AfterStream after_stream,
+                                          int trace_base = -1) {
+  constexpr int D = R / P;
+  constexpr int UNIT = P * kUnitPlaneBytes;
+  constexpr size_t WSTEP = (size_t)W * UNIT;
   constexpr int KPB = (WB == 1) ? 32 : 16;  // k per k-block
-  uint64_t* xbar = reinterpret_cast<uint64_t*>(smem);
-  volatile int* abort_flag = reinterpret_cast<int*>(smem + kOffMisc);
   float* rms_r = reinterpret_cast<float*>(smem + kOffMisc + 16);
   float* red = reinterpret_cast<float*>(smem + 128);
   float4* slots = reinterpret_cast<float4*>(smem + kOffSlots);  // [n_slots][W][P][32]
   __half* xs = reinterpret_cast<__half*>(smem + p.off_x);
-
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q = lane & 3;
-  const int M = p.M;
-  const int kbpv = p.kbpv;
-  const long long T = p.total_units;
-  const int G = p.grid;
-  const int u0 = (int)((long long)blockIdx.x * T / G);
-  const int u1 = (int)((long long)(blockIdx.x + 1) * T / G);
-  const int n_units = u1 - u0;
-  if (n_units <= 0) return;  // whole CTA: no barrier is reached
-  if (tid == 0) TRACE(0);
-  const int n_mine = n_units > warp ? (n_units - warp + W - 1) / W : 0;  // units u0 + warp + j*W
-
-  // ---- weight stream: the first D units, before waiting on the previous kernel
-  const uint64_t pol = l2_policy_evict_first();
-  const uint8_t* wlane = p.packed + ((size_t)u0 + warp) * UNIT + lane * 16;
-  constexpr size_t WSTEP = (size_t)W * UNIT;
-  uint4 buf[D][P];
-#pragma unroll
-  for (int d = 0; d < D; ++d)
-    if (d < n_mine) {
-#pragma unroll
-      for (int pl = 0; pl < P; ++pl) buf[d][pl] = ldg_stream(wlane + d * WSTEP + pl * kUnitPlaneBytes, pol);
-    }
-
-  if (tid == 0) {
-    mbar_init(xbar, 1);
-    *abort_flag = 0;
-    fence_mbarrier_init();
-    pdl_launch_dependents();
-  }
-  for (int i = tid; i < p.n_slots * W * P * 32; i += NT) slots[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-
-  // ---- the x rows this CTA needs
+  const int M = p.M, kbpv = p.kbpv;
+  const Range r = cta_range(p, warp);
+  const int u0 = r.u0, n_mine = r.n_mine;
+  const bool active = r.u1 > r.u0;
   const int vt_first = u0 / kbpv;
-  const int vt_last = (u1 - 1) / kbpv;
-  const int ks_lo = vt_first / p.n_tiles, ks_hi = vt_last / p.n_tiles;
-  const int k_lo = ks_lo * kbpv * KPB;
-  const int krange = (ks_hi + 1 - ks_lo) * kbpv * KPB;
+  const int vt_last = active ? (r.u1 - 1) / kbpv : vt_first - 1;
+  const int k_lo = (vt_first / p.n_tiles) * kbpv * KPB;
+  const int krange = active ? (vt_last / p.n_tiles + 1 - vt_first / p.n_tiles) * kbpv * KPB : 0;
+
+  // ---- activations
+  if (tid == 0) STRACE(trace_base);
+  if (active) stage_x(p, io, xs, k_lo, krange, tid);
+  for (int i = tid; i < p.n_slots * W * P * 32; i += NT) slots[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   __syncthreads();
-  pdl_wait();
-  if (tid == 0) TRACE(1);
-  if (p.x_tma) {
-    if (tid == 0) {
-      fence_proxy_async_global();
-      const uint32_t row_bytes = (uint32_t)krange * 2;
-      mbar_arrive_expect_tx(xbar, row_bytes * M);
-      const uint64_t keep = l2_policy_evict_last();
-      for (int m = 0; m < M; ++m)
-        bulk_g2s(xs + (size_t)m * p.x_rs, p.x + (size_t)m * p.ldx + k_lo, row_bytes, xbar, keep);
-    }
-    if (!__all_sync(0xffffffffu, mbar_wait_bounded(xbar, 0))) {
-      if (lane == 0) {
-        atomicCAS(p.error, 0, kErrFullWait);
-        *abort_flag = 1;
-      }
-    }
-  } else {
-    stage_x_manual(p, xs, k_lo, krange, tid);
-  }
-  __syncthreads();
-  if (p.rmsnorm) {
+  if (p.rmsnorm && active) {
     rmsnorm_rows(p, xs, rms_r, red, tid);
     __syncthreads();
   }
-  if (tid == 0) TRACE(2);
+  if (threadIdx.x == 0) {
+    TRACE(2);
+    STRACE(trace_base + 1);
+  }
 
   // ---- stream: compute unit j while units j+1 .. j+D-1 are in flight
   using Math = typename std::conditional<MATH == kMathMma, MmaMath<P, WB>, FfmaMath<P, WB>>::type;
   Math math;
   math.zero();
   // Segment bookkeeping: this warp's units in the current virtual tile are
-  // counted down (seg_left) instead of re-deriving the tile per unit.
+  // counted down; the tile is re-derived only at a segment end.
   int vt = (u0 + warp) / kbpv;
-  int kbl = (u0 + warp) - vt * kbpv;  // k-block (within vt) of the segment's first unit
+  int kbl = (u0 + warp) - vt * kbpv;     // k-block (within vt) of the segment's first unit
   int seg_n = (kbpv - kbl + W - 1) / W;  // this warp's units in vt
   int seg_left = seg_n;
   int cur_j = vt - vt_first;
-  // This lane's slice of the staged x: the prepack permutes k inside each
-  // block so the B fragment is one 16 B (E4M3) or 8 B (FP16) load at
-  // k-offset 8q (4q) of row g.  xoff: k offset of the warp's next unit.
+  // This lane's B fragment: row g of the staged x at k-offset 8q (E4M3) or
+  // 4q (FP16) of each block (the prepack's k permutation).  Rows g >= M read
+  // row 0: those token columns are computed but never stored.
   const __half* xlane = xs + (size_t)(g < M ? g : 0) * p.x_rs + (WB == 1 ? 8 * q : 4 * q);
   const __half* xq = xs + (WB == 1 ? 8 * q : 4 * q);  // row 0, for the FFMA variant
-  int xoff = ((vt / p.n_tiles) * kbpv + kbl) * KPB - k_lo;
-  const uint8_t* lp = wlane + D * WSTEP;  // address of unit j + D
-  int loads_left = n_mine - D;
+  int xoff = ((vt / p.n_tiles) * kbpv + kbl) * KPB - k_lo;  // k offset (halves) of the next unit
+  uint32_t xa = smem_addr(xlane) + 2 * xoff;                  // its shared address
+  const uint8_t* lp = io.packed + ((size_t)u0 + warp) * UNIT + lane * 16 + D * WSTEP;  // unit j0 + D
 
   auto flush = [&](int j) {
     float v[P][4];
@@ -506,69 +569,69 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int pl = 0; pl < P; ++pl)
       slots[((size_t)(j * W + warp) * P + pl) * 32 + lane] = make_float4(v[pl][0], v[pl][1], v[pl][2], v[pl][3]);
   };
-
-  for (int j0 = 0; j0 < n_mine; j0 += D) {
-#pragma unroll
-    for (int d = 0; d < D; ++d) {
-      if (j0 + d < n_mine) {
-        uint4 xf = make_uint4(0, 0, 0, 0);
-        if constexpr (MATH == kMathMma) {
-          if (g < M) {
-            if constexpr (WB == 1) {
-              xf = lds128(xlane + xoff);
-            } else {
-              const uint2 t = lds64(xlane + xoff);
-              xf.x = t.x;
-              xf.y = t.y;
-            }
-          }
-          math.unit(buf[d], xf);
-        } else {
-          math.unit(buf[d], xq + xoff, M, p.x_rs);
-        }
-        if (loads_left > 0) {
-#pragma unroll
-          for (int pl = 0; pl < P; ++pl) buf[d][pl] = ldg_stream(lp + pl * kUnitPlaneBytes, pol);
-          lp += WSTEP;
-        }
-        --loads_left;
-        xoff += W * KPB;
-        if (--seg_left == 0) {
-          // this warp's next virtual tile: unit vt*kbpv + kbl + seg_n*W
-          flush(cur_j);
-          math.zero();
-          kbl += seg_n * W - kbpv;
-          ++vt;
-          while (kbl >= kbpv) {
-            kbl -= kbpv;
-            ++vt;
-          }
-          seg_n = (kbpv - kbl + W - 1) / W;
-          seg_left = seg_n;
-          cur_j = vt - vt_first;
-          xoff = ((vt / p.n_tiles) * kbpv + kbl) * KPB - k_lo;
-        }
+  // Unit d of the current block: math on ring slot d, then (if `load`) refill
+  // the slot with the unit D ahead.
+  auto unit = [&](const int d, const bool load) {
+    if constexpr (MATH == kMathMma) {
+      uint4 xf;
+      if constexpr (WB == 1) {
+        xf = lds128_at(xa);
+      } else {
+        const uint2 t = lds64_at(xa);
+        xf = make_uint4(t.x, t.y, 0u, 0u);
       }
+      math.unit(&ring[d * P], xf);
+    } else {
+      math.unit(&ring[d * P], xq + xoff, M, p.x_rs);
     }
+    if (load) {
+#pragma unroll
+      for (int pl = 0; pl < P; ++pl)
+        ring[d * P + pl] = ldg_stream(lp + (size_t)d * WSTEP + pl * kUnitPlaneBytes, pol);
+    }
+    xoff += W * KPB;
+    xa += 2 * W * KPB;
+    if (--seg_left == 0) {
+      // this warp's next virtual tile: unit vt*kbpv + kbl + seg_n*W
+      flush(cur_j);
+      math.zero();
+      kbl += seg_n * W - kbpv;
+      ++vt;
+      while (kbl >= kbpv) {
+        kbl -= kbpv;
+        ++vt;
+      }
+      seg_n = (kbpv - kbl + W - 1) / W;
+      seg_left = seg_n;
+      cur_j = vt - vt_first;
+      xoff = ((vt / p.n_tiles) * kbpv + kbl) * KPB - k_lo;
+      xa = smem_addr(xlane) + 2 * xoff;
+    }
+  };
+  // Whole blocks of D units (slot d of a block refills with unit j0 + D + d
+  // while that exists), then the last partial block, which loads nothing.
+  const int n_full = n_mine - n_mine % D;
+  int j0 = 0;
+  for (; j0 < n_full; j0 += D) {
+    const int lim = n_mine - D - j0;
+#pragma unroll
+    for (int d = 0; d < D; ++d) unit(d, d < lim);
+    lp += (size_t)D * WSTEP;
+  }
+  if (j0 < n_mine) {
+#pragma unroll
+    for (int d = 0; d < D; ++d)
+      if (j0 + d < n_mine) unit(d, false);
   }
   if (n_mine > 0 && seg_left != seg_n) flush(cur_j);
-  if (tid == 0) {
+  if (threadIdx.x == 0) {
     TRACE(3);
-    // Warm L2 with the start of the range the next kernel's CTA of the same
-    // index will stream.
-    if (p.pf_packed != nullptr && (int)blockIdx.x < p.pf_grid) {
-      const long long a = (long long)blockIdx.x * p.pf_total_units / p.pf_grid;
-      const long long b = (long long)(blockIdx.x + 1) * p.pf_total_units / p.pf_grid;
-      const long long bytes = min((long long)p.pf_bytes, (b - a) * p.pf_unit_bytes);
-      const uint8_t* src = p.pf_packed + a * p.pf_unit_bytes;
-      for (long long off = 0; off < bytes; off += 32768)
-        bulk_prefetch_l2(src + off, (uint32_t)min(32768LL, bytes - off));
-    }
+    STRACE(trace_base + 2);
   }
+  after_stream(ring);
 
   // ---- combine: the warps' partials in warp order, then finish each tile
   __syncthreads();
-  if (*abort_flag) return;
   const int nvt = vt_last - vt_first + 1;
   for (int j = warp; j < nvt; j += W) {
     float v[P][4];
@@ -584,8 +647,132 @@ __global__ void __launch_bounds__(kThreads, 1)
         v[pl][3] += t.w;
       }
     }
-    finish_vt<P>(p, vt_first + j, v, lane);
+    finish_vt<P>(p, io, vt_first + j, v, lane);
   }
+#ifdef B2G_TRACE
+  __syncthreads();
+  if (tid == 0) STRACE(trace_base + 3);
+#endif
+}
+
+// ---------------------------------------------------------------------------
+// One GEMV per launch
+// ---------------------------------------------------------------------------
+template <int P, int WB, int MATH>
+__global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_constant__ GemvParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  // 128 KB of weights in flight per SM (16 B x 512 threads x 16); the FFMA
+  // variant needs the registers for its accumulators and keeps half.
+  constexpr int R = (MATH == kMathMma) ? kRing : kRing / 2;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) TRACE(0);
+  const uint64_t pol = l2_policy_evict_first();
+  uint4 ring[R];
+  // Weights are constant: the first loads go out before the previous kernel
+  // in the stream is waited on.
+  prefetch_phase<P, R>(p, p.packed, ring, warp, lane, pol);
+  // Warm L2 with the range the next kernel's CTA of the same index will
+  // stream, so HBM keeps working through this kernel's tail and the launch gap.
+  if (tid == 0 && p.pf_packed != nullptr && (int)blockIdx.x < p.pf_grid) {
+    const long long a = (long long)blockIdx.x * p.pf_total_units / p.pf_grid;
+    const long long b = (long long)(blockIdx.x + 1) * p.pf_total_units / p.pf_grid;
+    const long long bytes = min((long long)p.pf_bytes, (b - a) * p.pf_unit_bytes);
+    const uint8_t* src = p.pf_packed + a * p.pf_unit_bytes;
+    for (long long off = 0; off < bytes; off += 32768)
+      bulk_prefetch_l2(src + off, (uint32_t)min(32768LL, bytes - off));
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+  if (tid == 0) TRACE(1);
+  run_phase<P, WB, MATH, R>(p, io_of_params(p), smem, ring, pol, [](uint4 (&)[R]) {});
+  if (tid == 0) TRACE(4);
+}
+
+// ---------------------------------------------------------------------------
+// The decode-MLP stack in one cooperative launch
+// ---------------------------------------------------------------------------
+// Grid barrier on a counter that is zero at launch and counts one arrival per
+// CTA per barrier: barrier b (1-based) completes when it reaches b * grid.
+// The wait is bounded; on expiry the error word is set and false returned.
+__device__ bool grid_barrier(unsigned* counter, unsigned target, int* err, volatile int* verdict) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    fence_acq_rel_gpu();
+    atomicAdd(counter, 1u);
+    const unsigned long long t0 = globaltimer_ns();
+    int ok = 1;
+    while (true) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
+      if (v >= target) break;
+      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+        atomicCAS(err, 0, kErrGridWait);
+        ok = 0;
+        break;
+      }
+      __nanosleep(32);
+    }
+    *verdict = ok;
+  }
+  __syncthreads();
+  return *verdict != 0;
+}
+
+// Last arrival of the launch: the CTA that brings the counter to `total`
+// (every CTA has passed every barrier) resets it for the next launch.
+__device__ void grid_exit(unsigned* counter, unsigned total) {
+  if (threadIdx.x == 0) {
+    const unsigned old = atomicAdd(counter, 1u);
+    if (old == total - 1) atomicExch(counter, 0u);
+  }
+}
+
+// The stack kernel keeps HBM busy independently of its phase structure: at
+// the start of each phase every CTA asks L2 to fetch its whole range of the
+// NEXT phase's weights (bulk prefetch through the TMA unit: no registers, no
+// L1 miss slots).  By the time the next phase streams, most of its weights
+// are L2 hits, and HBM works through the following phase meanwhile.  L2 holds
+// at most two phases (75 MB of a Llama-3.2-3B layer) at once.
+constexpr long long kWholeRange = 1LL << 40;
+
+template <int WB>
+__global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constant__ StackParams sp) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  constexpr int R = kRing;
+  volatile int* verdict = reinterpret_cast<int*>(smem + kOffMisc);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint64_t pol = l2_policy_evict_first();
+  const GemvParams& gu = sp.gu;
+  const GemvParams& dn = sp.dn;
+  const unsigned G = gridDim.x;
+  uint4 ring[R];
+  unsigned nbar = 0;
+  if (tid == 0) TRACE(0);
+  l2_prefetch_phase(gu, sp.layers[0].pgu, 2 * kUnitPlaneBytes, kWholeRange);
+  prefetch_phase<2, R>(gu, sp.layers[0].pgu, ring, warp, lane, pol);
+  for (int l = 0; l < sp.n_layers; ++l) {
+    const StackLayer& L = sp.layers[l];
+    const bool more = l + 1 < sp.n_layers;
+    const uint8_t* next_gu = more ? sp.layers[l + 1].pgu : nullptr;
+    // act = SiLU(RMSNorm(h) . Wg) * (RMSNorm(h) . Wu); this layer's down
+    // weights go to L2 meanwhile.
+    l2_prefetch_phase(dn, L.pd, kUnitPlaneBytes, kWholeRange);
+    const Io io_gu{L.pgu, L.sgu, sp.h, sp.ldh, nullptr, 0, sp.act, sp.ldact};
+    run_phase<2, WB, kMathMma, R>(gu, io_gu, smem, ring, pol, [](uint4 (&)[R]) {}, 8 * l);
+    // The ring is free again: the down phase's first units load while the
+    // barrier completes.
+    prefetch_phase<1, R>(dn, L.pd, ring, warp, lane, pol);
+    if (!grid_barrier(sp.barrier, (++nbar) * G, gu.error, verdict)) return;
+    // h = h + act . Wd; the next layer's gate||up weights go to L2 meanwhile.
+    if (more) l2_prefetch_phase(gu, next_gu, 2 * kUnitPlaneBytes, kWholeRange);
+    const Io io_dn{L.pd, L.sd, sp.act, sp.ldact, sp.h, sp.ldh, sp.h, sp.ldh};
+    run_phase<1, WB, kMathMma, R>(dn, io_dn, smem, ring, pol, [](uint4 (&)[R]) {}, 8 * l + 4);
+    if (more) {
+      prefetch_phase<2, R>(gu, next_gu, ring, warp, lane, pol);
+      if (!grid_barrier(sp.barrier, (++nbar) * G, gu.error, verdict)) return;
+    }
+  }
+  grid_exit(sp.barrier, (nbar + 1) * G);
   if (tid == 0) TRACE(4);
 }
 
@@ -602,12 +789,6 @@ cudaError_t launch_variant(const GemvParams& p, size_t smem, bool pdl, cudaStrea
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH>, p);
-}
-
-template <int P, int WB, int MATH>
-cudaError_t set_limit(int bytes) {
-  return cudaFuncSetAttribute(gemv_streamk_kernel<P, WB, MATH>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 }  // namespace
@@ -628,25 +809,54 @@ cudaError_t launch_gemv(const GemvParams& p, int planes, int wbytes, int math, s
   return cudaErrorInvalidValue;
 }
 
+cudaError_t launch_stack(const StackParams& sp, int wbytes, size_t smem, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sp.gu.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (wbytes == 1) return cudaLaunchKernelEx(&cfg, stack_kernel<1>, sp);
+  if (wbytes == 2) return cudaLaunchKernelEx(&cfg, stack_kernel<2>, sp);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t stack_max_coresident(int wbytes, size_t smem, int num_sms, int* max_grid) {
+  int per_sm = 0;
+  const cudaError_t e =
+      wbytes == 1 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stack_kernel<1>, kThreads, smem)
+                  : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stack_kernel<2>, kThreads, smem);
+  *max_grid = per_sm * num_sms;
+  return e;
+}
+
 #ifdef B2G_TRACE
 extern "C" int b2g_debug_trace(unsigned long long* out, int n_ctas) {
   return (int)cudaMemcpyFromSymbol(out, g_trace, sizeof(unsigned long long) * 16 * n_ctas);
 }
-
+extern "C" int b2g_debug_stack_trace(unsigned long long* out, int n_ctas) {
+  return (int)cudaMemcpyFromSymbol(out, g_strace, sizeof(unsigned long long) * kTracePts * n_ctas);
+}
 #endif
 
 cudaError_t gemv_set_smem_limit(int bytes) {
   cudaError_t e = cudaSuccess, r;
-#define B2G_LIM(PP, WBB, MM) \
-  if ((r = set_limit<PP, WBB, MM>(bytes)) != cudaSuccess) e = r;
-  B2G_LIM(1, 1, kMathMma)
-  B2G_LIM(2, 1, kMathMma)
-  B2G_LIM(1, 2, kMathMma)
-  B2G_LIM(2, 2, kMathMma)
-  B2G_LIM(1, 1, kMathFfma)
-  B2G_LIM(2, 1, kMathFfma)
-  B2G_LIM(1, 2, kMathFfma)
-  B2G_LIM(2, 2, kMathFfma)
+#define B2G_LIM(K) \
+  if ((r = cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes)) != cudaSuccess) e = r;
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma>))
+  B2G_LIM((stack_kernel<1>))
+  B2G_LIM((stack_kernel<2>))
 #undef B2G_LIM
   return e;
 }

@@ -22,15 +22,17 @@ constexpr int kTileCh = 16;
 constexpr int kWarps = 16;  // one CTA of 16 warps per SM
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxSlots = 8;  // virtual tiles one CTA may touch
-// Shared memory: [0,8) x barrier, [64,80) flags, [80,112) RMS factors,
-// [128,640) RMSNorm partial sums, then the per-warp partial slots
+// Shared memory: [64,68) barrier verdict, [80,112) RMS factors, [128,640)
+// RMSNorm partial sums, then the per-warp partial slots
 // [n_slots][warps][planes][32 lanes][16 B], then the x rows.
 constexpr int kOffMisc = 64;
 constexpr int kOffSlots = 1024;
 // Workspace: tile counters first (fixed size, so ops sharing one workspace
-// agree on where they are), then the split-K partials.
+// agree on where they are), then the split-K partials.  The last 256 bytes of
+// the counter region hold the stack kernel's grid-barrier counter.
 constexpr int kCounterRegionBytes = 65536;
-constexpr int kMaxTiles = kCounterRegionBytes / 4;
+constexpr int kBarrierWordOffset = kCounterRegionBytes - 256;
+constexpr int kMaxTiles = kBarrierWordOffset / 4;
 
 enum MathKind : int { kMathMma = 0, kMathFfma = 1 };
 
@@ -47,6 +49,8 @@ struct GemvParams {
   int* counters;    // [n_tiles], zero between calls
   int* error;
   long long total_units;
+  double r_units;  // 1.0 / total_units and 1.0 / grid (exact floor divisions, see floor_div)
+  double r_grid;
   int grid;
   int n_tiles;
   int kb_total;  // k-blocks (32 k for E4M3, 16 k for FP16) over padded K
@@ -61,7 +65,6 @@ struct GemvParams {
   int n_slots;    // max virtual tiles per CTA (<= kMaxSlots)
   int off_x;      // shared-memory byte offset of the x rows
   int x_rs;       // x row stride in shared memory (halves)
-  int x_tma;      // 1: stage x with bulk copies (aligned rows, K % 32 == 0)
   // L2 prefetch of the next kernel's stream: CTA c prefetches the first
   // pf_bytes of the range the next kernel's CTA c will stream (0 = off).
   const uint8_t* pf_packed;
@@ -74,6 +77,32 @@ struct GemvParams {
 // Launch one GEMV (planes = 1 or 2, wbytes = 1 for E4M3 or 2 for FP16).
 cudaError_t launch_gemv(const GemvParams& p, int planes, int wbytes, int math, size_t smem,
                         bool pdl, cudaStream_t stream);
+
+// The decode-MLP stack in one cooperative launch.  Per layer l: phase 1 =
+// gu (RMSNorm(h) -> gate||up -> SiLU*up -> act), phase 2 = dn (act -> down ->
+// h += .), grid barriers between phases.  gu / dn hold each phase's plan and
+// workspace pointers; their packed / x / y / scales / residual fields are
+// unused (taken from layers, h and act).
+constexpr int kMaxStackLayers = 32;  // per launch; the host chunks longer stacks
+struct StackLayer {
+  const uint8_t* pgu;
+  const void* sgu;
+  const uint8_t* pd;
+  const void* sd;
+};
+struct StackParams {
+  GemvParams gu, dn;
+  StackLayer layers[kMaxStackLayers];
+  __half* h;
+  long long ldh;
+  __half* act;
+  long long ldact;
+  unsigned* barrier;  // zero at launch; the kernel leaves it zero
+  int n_layers;
+};
+cudaError_t launch_stack(const StackParams& sp, int wbytes, size_t smem, cudaStream_t stream);
+// Largest grid of stack_kernel<wbytes> that can be co-resident with `smem` bytes per CTA.
+cudaError_t stack_max_coresident(int wbytes, size_t smem, int num_sms, int* max_grid);
 // Raises the dynamic shared-memory limit of every kernel variant.
 cudaError_t gemv_set_smem_limit(int bytes);
 

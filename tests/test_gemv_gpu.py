@@ -285,3 +285,43 @@ def test_stack_full_28_layers(b2g, orc, syn, cuda):
     r = orc.compare(host(h), want.astype(np.float64))
     assert r["rel_l2"] <= 5e-3, r
     assert b2g.device_error() == 0
+
+
+@pytest.mark.parametrize("wd", [0, 1])
+@pytest.mark.parametrize("hidden,inter,n_layers", [(256, 512, 3), (3072, 8192, 2), (96, 160, 33)])
+def test_stack_persistent_matches_per_layer(b2g, orc, syn, cuda, wd, hidden, inter, n_layers):
+    """The one-launch stack kernel and the per-layer launches compute the same
+    partition in the same order: bitwise-identical hidden states.  33 layers
+    exercise the host's split into launches of at most 32 layers."""
+    mode = 3 if wd else 0
+    st, _ = build_stack(b2g, orc, syn, hidden, inter, n_layers, wd, mode)
+    ws = st.workspace()
+    for M in (1, 3, 8):
+        h0 = dev(syn.hidden_state(M, hidden))
+        out = {}
+        for m in ("per_layer", "persistent", "per_layer", "persistent"):
+            st.set_mode(m)
+            h = h0.clone()
+            act = torch.empty((M, inter), dtype=torch.float16, device="cuda")
+            st.enqueue(h, act, ws)
+            torch.cuda.synchronize()
+            if m in out:
+                assert torch.equal(out[m], h), (m, M)
+            out[m] = h
+        assert torch.equal(out["per_layer"], out["persistent"]), M
+    assert b2g.device_error() == 0
+    # Counters and the grid-barrier word are back to zero.
+    assert int(ws[:65536].count_nonzero()) == 0
+
+
+def test_stack_persistent_full_vs_oracle(b2g, orc, syn, cuda):
+    st, layers = build_stack(b2g, orc, syn, 3072, 8192, 4)
+    st.set_mode("persistent")
+    for M in (1, 8):
+        h0 = syn.hidden_state(M)
+        h = dev(h0)
+        act = torch.empty((M, 8192), dtype=torch.float16, device="cuda")
+        st.enqueue(h, act, st.workspace())
+        torch.cuda.synchronize()
+        want = orc.mlp_stack(h0, layers)
+        check(orc, h, want.astype(np.float64), 1, M)
