@@ -114,9 +114,10 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # Weights
 # ---------------------------------------------------------------------------
-def make_layers(b2g, torch, device, tp: int, rank: int, ops, M: int):
+def make_layers(b2g, torch, device, tp: int, rank: int, ops, M: int, keep_raw: bool = False):
     """28 layers of N(0, 0.02) weights, E4M3 per-channel FP32 (quantised over
-    the full matrix, then sharded), prepacked for this rank."""
+    the full matrix, then sharded), prepacked for this rank.  keep_raw keeps
+    every layer's raw [K, N] E4M3 codes (the reference kernels' layout)."""
     gu_op, dn_op = ops
     inter = INTER // tp
     cs = slice(rank * inter, (rank + 1) * inter)
@@ -135,8 +136,85 @@ def make_layers(b2g, torch, device, tp: int, rank: int, ops, M: int):
         sgu = torch.cat([sg[cs], su[cs]]).contiguous()
         pd = dn_op.prepack(qd[cs, :].contiguous())
         layers.append({"pgu": pgu, "sgu": sgu, "pd": pd, "sd": sd,
-                       "q0": (qg, qu, qd) if l == 0 else None})
+                       "q0": (qg, qu, qd) if (l == 0 or keep_raw) else None})
     return layers
+
+
+# ---------------------------------------------------------------------------
+# The reference's own GPU kernels (kernels/gemv_fp8.cu run_gemv, compiled for
+# sm_100a by baseline/Makefile) on the same weights
+# ---------------------------------------------------------------------------
+REF_GPU_LIB = ROOT / "baseline" / "_ref" / "libref_gpu.so"
+
+
+def reference_kernels(torch, layers, h, M: int, our_ms_per_step: float):
+    """Times the reference GEMV path on the 28-layer stack: per layer and token
+    its three M=1 GEMVs (gate, up, down; memset + gemv_chunk_kernel + cast
+    each, kernels/gemv_fp8.cu:276-283), M tokens one after another (the
+    reference has no M>1 path), weights rotating over the 28 distinct layers.
+    RMSNorm, SiLU*up and the residual are not counted (the reference has no
+    kernels for them).  Variant/grid/KU: the best of a sweep on this GPU over
+    the reference's own knobs, and its shipped L4 setting for comparison."""
+    import ctypes
+    if not REF_GPU_LIB.exists():
+        return {"unavailable": "baseline/_ref/libref_gpu.so not built (make -C baseline needs the reference sources)"}
+    L = ctypes.CDLL(str(REF_GPU_LIB))
+    L.ref_gpu_gemv_fp8.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 5
+    dev = h.device
+    x = h[0].contiguous()
+    a = torch.randn(INTER, device=dev).half()
+    y_acc = torch.empty(INTER, dtype=torch.float32, device=dev)
+    y = torch.empty(INTER, dtype=torch.float16, device=dev)
+
+    def gemv(w, xv, K, N, cfg):
+        st = L.ref_gpu_gemv_fp8(w.data_ptr(), xv.data_ptr(), y_acc.data_ptr(), y.data_ptr(), K, N, *cfg)
+        if st != 0:
+            raise RuntimeError(f"reference gemv failed: CUDA error {st}")
+
+    def timed(fn, reps):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    shapes = {"gate_up": (HIDDEN, INTER, 0, x), "down": (INTER, HIDDEN, 2, a)}
+    best, shipped = {}, {}
+    for name, (K, N, j, xv) in shapes.items():
+        ws = [layers[l]["q0"][j] for l in range(LAYERS)]
+
+        def sweep_one(cfg):
+            return timed(lambda: [gemv(w, xv, K, N, cfg) for w in ws], 2) * 1e3 / LAYERS
+        shipped_cfg = (L.ref_gpu_fp8_best_variant(), L.ref_gpu_fp8_best_grid(N), L.ref_gpu_fp8_best_ku(N))
+        sweep_one(shipped_cfg)
+        shipped[name] = {"cfg": shipped_cfg, "us": round(sweep_one(shipped_cfg), 2)}
+        results = []
+        for variant in range(4):
+            for grid in (20, 48, 96, 148, 296, 592):
+                for ku in (2, 4, 8):
+                    results.append((sweep_one((variant, grid, ku)), (variant, grid, ku)))
+        us, cfg = min(results)
+        best[name] = {"cfg": cfg, "us": round(us, 2)}
+
+    def step():
+        for l in range(LAYERS):
+            qg, qu, qd = layers[l]["q0"]
+            for _ in range(M):
+                gemv(qg, x, HIDDEN, INTER, best["gate_up"]["cfg"])
+                gemv(qu, x, HIDDEN, INTER, best["gate_up"]["cfg"])
+                gemv(qd, a, INTER, HIDDEN, best["down"]["cfg"])
+    step()
+    ms = timed(step, 3)
+    return {"what": "reference kernels/gemv_fp8.cu run_gemv (memset + gemv_chunk_kernel + cast), sm_100a build, "
+                    f"3 GEMVs x {M} tokens x {LAYERS} layers per step, best sweep config",
+            "ms_per_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / LAYERS, 2),
+            "per_gemv_us_best": {k: v["us"] for k, v in best.items()},
+            "best_cfg_variant_grid_ku": {k: v["cfg"] for k, v in best.items()},
+            "per_gemv_us_shipped_l4_cfg": {k: v["us"] for k, v in shipped.items()},
+            "ours_speedup": round(ms / our_ms_per_step, 2)}
 
 
 # ---------------------------------------------------------------------------
@@ -212,16 +290,18 @@ def run_ours(args):
         # One GPU: the library's stack (one cooperative launch for all layers).
         st = b2g.Stack(HIDDEN, INTER, LAYERS, max_m=M)
         gu_op, dn_op = st.gate_up, st.down
+        tps = None
     else:
+        # Tensor parallel: the package's TPStack (column/K shards, residual on
+        # rank 0, NCCL all-reduce of the partials per layer).
+        import importlib
         st = None
-        gu_op = b2g.GemvOp(HIDDEN, inter, max_m=M,
-                           fuse=b2g.FUSE_GATE_UP_SILU | b2g.FUSE_RMSNORM_INPUT)
-        dn_op = b2g.GemvOp(inter, HIDDEN, max_m=M,
-                           fuse=b2g.FUSE_RESIDUAL_ADD if rank == 0 else b2g.FUSE_NONE)
-    layers = make_layers(b2g, torch, device, tp, rank, (gu_op, dn_op), M)
-    if st is not None:
-        for i, L in enumerate(layers):
-            st.set_layer(i, L["pgu"], L["sgu"], L["pd"], L["sd"])
+        tps = importlib.import_module("b2g.tp").TPStack(HIDDEN, INTER, LAYERS, rank=rank, world=world, max_m=M)
+        gu_op, dn_op = tps.gate_up, tps.down
+    want_ref = tp == 1 and not args.no_ref_kernels and REF_GPU_LIB.exists()
+    layers = make_layers(b2g, torch, device, tp, rank, (gu_op, dn_op), M, keep_raw=want_ref)
+    for i, L in enumerate(layers):
+        (st or tps).set_layer(i, L["pgu"], L["sgu"], L["pd"], L["sd"])
     torch.cuda.synchronize()
 
     stream = torch.cuda.current_stream()
@@ -235,14 +315,7 @@ def run_ours(args):
     ws.zero_()
 
     def step_ops():
-        for i, L in enumerate(layers):
-            nxt = layers[(i + 1) % LAYERS]
-            gu_op.enqueue(h, L["pgu"], L["sgu"], y=act, workspace=ws, pdl=True,
-                          prefetch=(dn_op, L["pd"]))
-            dn_op.enqueue(act, L["pd"], L["sd"], y=h, residual=h if rank == 0 else None,
-                          workspace=ws, pdl=True, prefetch=(gu_op, nxt["pgu"]))
-            if tp > 1:
-                dist.all_reduce(h)
+        tps.enqueue(h, act, ws)
 
     def step_stack():
         st.enqueue(h, act, ws)
@@ -369,6 +442,11 @@ def run_ours(args):
     ms_e2e = timed(e2e_step, k_e2e) / k_e2e
     e2e_value = bytes_rank * tp / (ms_e2e * 1e-3) / 1e12
 
+    # ---- the reference's own GPU kernels on the same weights (one GPU)
+    ref_k = None
+    if tp == 1 and not args.no_ref_kernels:
+        ref_k = reference_kernels(torch, layers, h0, M, ms_step)
+
     # ---- CPU baseline (rank 0 at N=1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -406,6 +484,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "detail": {
                 **detail_extra,
+                "reference_kernels_sm100": ref_k,
                 "direct_launch_ms_per_step": round(ms_direct / args.steps, 5),
                 "gate_up_us_per_launch": round(ms_gu * 1e3, 3),
                 "gate_up_alg_bytes": gu_b,
@@ -473,6 +552,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-ref-kernels", action="store_true", help="skip timing the reference's GPU kernels")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -135,8 +135,14 @@ b2g_status b2g_destroy(b2g_op* op);
  * kernels/gemv_fp8.cu:820-901, become per-op options).
  *  B2G_OPT_MATH: 0 = tensor-core m16n8k16 tiles (default),
  *                1 = CUDA-core FFMA with the same data layout.
- *  B2G_OPT_GRID: CTA count, 0 = one per SM (default). */
-enum { B2G_OPT_MATH = 1, B2G_OPT_GRID = 2 };
+ *  B2G_OPT_GRID: CTA count, 0 = one per SM (default).
+ *  B2G_OPT_PARTITION: how the weight stream is cut among the CTAs:
+ *    UNITS = equal byte ranges (a 16-channel tile may be split between two
+ *    CTAs, which then combine partial sums); TILES = whole tiles per CTA (no
+ *    split, up to one tile of imbalance); AUTO (default) = TILES when K is
+ *    not split and the imbalance is at most 20%, else UNITS. */
+enum { B2G_OPT_MATH = 1, B2G_OPT_GRID = 2, B2G_OPT_PARTITION = 3 };
+enum { B2G_PARTITION_AUTO = 0, B2G_PARTITION_UNITS = 1, B2G_PARTITION_TILES = 2 };
 b2g_status b2g_op_set_option(b2g_op* op, int32_t key, int32_t value);
 
 /* The launch plan chosen for calls with m rows. */
@@ -150,6 +156,7 @@ typedef struct {
   int64_t inflight_bytes_per_cta; /* weight bytes each CTA keeps in flight */
   int64_t smem_bytes;       /* dynamic shared memory per CTA */
   int32_t max_contrib;      /* max CTAs sharing one virtual tile */
+  int32_t partition;        /* B2G_PARTITION_UNITS or _TILES, as planned */
   int32_t n_slots;          /* virtual tiles per CTA (max) */
   int32_t x_kblocks;        /* 32-wide k blocks of x staged per CTA */
   int32_t math;

@@ -25,7 +25,8 @@ DTYPE = {"fp16": 0, "fp8_e4m3": 1}
 SCALE = {"none": 0, "tensor_fp16": 1, "channel_fp16": 2, "channel_fp32": 3}
 LAYOUT = {"KN": 0, "NK": 1}
 FUSE_NONE, FUSE_GATE_UP_SILU, FUSE_RMSNORM_INPUT, FUSE_RESIDUAL_ADD = 0, 1, 2, 4
-OPT_MATH, OPT_GRID = 1, 2
+OPT_MATH, OPT_GRID, OPT_PARTITION = 1, 2, 3
+PARTITION_AUTO, PARTITION_UNITS, PARTITION_TILES = 0, 1, 2
 MATH_MMA, MATH_FFMA = 0, 1
 STACK_OPT_MODE = 1
 STACK_MODE_PERSISTENT, STACK_MODE_PER_LAYER = 0, 1
@@ -57,6 +58,7 @@ class PlanInfo(ctypes.Structure):
                 ("kblocks_per_vtile", ctypes.c_int32), ("n_tiles", ctypes.c_int32),
                 ("total_units", ctypes.c_int64), ("unit_bytes", ctypes.c_int32),
                 ("inflight_bytes_per_cta", ctypes.c_int64), ("smem_bytes", ctypes.c_int64), ("max_contrib", ctypes.c_int32),
+                ("partition", ctypes.c_int32),
                 ("n_slots", ctypes.c_int32), ("x_kblocks", ctypes.c_int32), ("math", ctypes.c_int32)]
 
     def as_dict(self):

@@ -28,6 +28,8 @@ struct b2g_op {
   size_t packed_bytes;
   int device, num_sms, smem_optin, smem_per_sm;
   int grid, grid_override;
+  int partition, gran;  // B2G_PARTITION_* requested; units per granule in use
+  long long total_gran;
   int max_contrib, n_slots, xk_cap;
   int math;
 };
@@ -66,16 +68,21 @@ b2g_status ensure_device_setup(int dev, int smem_optin) {
   return B2G_OK;
 }
 
-long long cta_of(long long u, long long T, int G) { return ((u + 1) * G + T - 1) / T - 1; }
+// The partition (mirrors cta_of / range_start in gemv.cu): CTA c streams
+// granules [c*Tg/G, (c+1)*Tg/G) of gran units each.
+long long range_start(const b2g_op* op, long long c) { return c * op->total_gran / op->grid * op->gran; }
+long long cta_of(const b2g_op* op, long long u) {
+  const long long Tg = op->total_gran;
+  return ((u / op->gran + 1) * op->grid + Tg - 1) / Tg - 1;
+}
 
-// Stream-K partition statistics for a grid of G CTAs.
+// Partition statistics for the op's grid.
 void plan_partition(b2g_op* op) {
-  const long long T = op->total_units;
   const int G = op->grid;
   int max_slots = 0, max_kx = 0;
   const int kx_per_ks = op->kbpv * op->kpb / 32;
   for (int c = 0; c < G; ++c) {
-    const long long u0 = (long long)c * T / G, u1 = (long long)(c + 1) * T / G;
+    const long long u0 = range_start(op, c), u1 = range_start(op, c + 1);
     if (u1 <= u0) continue;
     const long long vf = u0 / op->kbpv, vl = (u1 - 1) / op->kbpv;
     max_slots = std::max(max_slots, (int)(vl - vf + 1));
@@ -86,7 +93,7 @@ void plan_partition(b2g_op* op) {
   const long long n_vt = (long long)op->ksplit * op->n_tiles;
   for (long long vt = 0; vt < n_vt; ++vt) {
     const long long a = vt * op->kbpv;
-    max_contrib = std::max(max_contrib, (int)(cta_of(a + op->kbpv - 1, T, G) - cta_of(a, T, G)) + 1);
+    max_contrib = std::max(max_contrib, (int)(cta_of(op, a + op->kbpv - 1) - cta_of(op, a)) + 1);
   }
   op->n_slots = max_slots;
   op->xk_cap = max_kx;
@@ -94,7 +101,7 @@ void plan_partition(b2g_op* op) {
 }
 
 struct LaunchPlan {
-  int off_x, x_rs;
+  int off_epi, off_x, x_rs;
   size_t smem;
 };
 
@@ -107,14 +114,30 @@ bool plan_launch(const b2g_op* op, int m, LaunchPlan* lp) {
   const int x_rs = (krange + 63) / 64 * 64 + (op->wbytes == 1 ? 32 : 16);
   const size_t xbytes = ((size_t)m * x_rs * 2 + 127) / 128 * 128;
   const size_t slot_bytes = (size_t)op->n_slots * kWarps * op->planes * kUnitPlaneBytes;
-  lp->off_x = (int)(kOffSlots + slot_bytes);
+  const size_t epi_bytes = ((size_t)op->n_slots * (op->planes * 16 + 8 * 16) * 4 + 127) / 128 * 128;
+  lp->off_epi = (int)(kOffSlots + slot_bytes);
+  lp->off_x = (int)(lp->off_epi + epi_bytes);
   lp->x_rs = x_rs;
   lp->smem = lp->off_x + xbytes;
   return lp->smem <= (size_t)op->smem_optin;
 }
 
 b2g_status replan(b2g_op* op) {
-  op->grid = (int)std::min<long long>(op->total_units, op->grid_override > 0 ? op->grid_override : op->num_sms);
+  const long long n_vt = (long long)op->ksplit * op->n_tiles;
+  const int want = op->grid_override > 0 ? op->grid_override : op->num_sms;
+  bool aligned = op->partition == B2G_PARTITION_TILES;
+  if (op->partition == B2G_PARTITION_AUTO) {
+    // Whole virtual tiles per CTA remove the cross-CTA handshake of split
+    // tiles; take that when nothing is split along K anyway and the
+    // granularity costs at most ~20% of stream imbalance.
+    const long long g = std::min<long long>(n_vt, want);
+    aligned = op->ksplit == 1 && (double)((n_vt + g - 1) / g) / ((double)n_vt / g) <= 1.2;
+  }
+  op->gran = aligned ? op->kbpv : 1;
+  op->total_gran = op->total_units / op->gran;
+  op->grid = (int)std::min<long long>(op->total_gran, want);
+  // The kernels' partition arithmetic is 32-bit.
+  if ((op->total_gran + 2) * (long long)op->grid >= (1LL << 31)) return B2G_ERR_UNSUPPORTED;
   plan_partition(op);
   if (op->n_slots > kMaxSlots) return B2G_ERR_UNSUPPORTED;
   LaunchPlan lp;
@@ -130,13 +153,18 @@ void fill_plan(const b2g_op* op, int m, const LaunchPlan& lp, void* workspace, i
   p->partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterRegionBytes);
   p->error = g_err_word[dev];
   p->total_units = op->total_units;
-  p->r_units = 1.0 / (double)op->total_units;
-  p->r_grid = 1.0 / (double)op->grid;
+  p->gran = op->gran;
+  p->div_gran = make_fast_div((uint32_t)op->gran);
+  p->total_gran = (int)op->total_gran;
+  p->div_tg = make_fast_div((uint32_t)op->total_gran);
+  p->div_grid = make_fast_div((uint32_t)op->grid);
   p->grid = op->grid;
   p->n_tiles = op->n_tiles;
   p->kb_total = op->kb_total;
   p->ksplit = op->ksplit;
   p->kbpv = op->kbpv;
+  p->div_kbpv = make_fast_div((uint32_t)op->kbpv);
+  p->div_tiles = make_fast_div((uint32_t)op->n_tiles);
   p->M = m;
   p->K = op->K;
   p->N = op->N;
@@ -145,6 +173,7 @@ void fill_plan(const b2g_op* op, int m, const LaunchPlan& lp, void* workspace, i
   p->residual_add = (op->f.fuse & B2G_FUSE_RESIDUAL_ADD) ? 1 : 0;
   p->max_contrib = op->max_contrib;
   p->n_slots = op->n_slots;
+  p->off_epi = lp.off_epi;
   p->off_x = lp.off_x;
   p->x_rs = lp.x_rs;
 }
@@ -256,6 +285,10 @@ b2g_status b2g_op_set_option(b2g_op* op, int32_t key, int32_t value) {
       if (value < 0) return B2G_ERR_INVALID;
       op->grid_override = value;
       return replan(op);
+    case B2G_OPT_PARTITION:
+      if (value < B2G_PARTITION_AUTO || value > B2G_PARTITION_TILES) return B2G_ERR_INVALID;
+      op->partition = value;
+      return replan(op);
   }
   return B2G_ERR_INVALID;
 }
@@ -273,6 +306,7 @@ b2g_status b2g_op_query(const b2g_op* op, int32_t m, b2g_plan_info* info) {
   info->inflight_bytes_per_cta = (int64_t)kThreads * 16 * (op->planes == 1 ? 16 : 16);
   info->smem_bytes = (int64_t)lp.smem;
   info->max_contrib = op->max_contrib;
+  info->partition = op->gran == 1 ? B2G_PARTITION_UNITS : B2G_PARTITION_TILES;
   info->n_slots = op->n_slots;
   info->x_kblocks = op->xk_cap;
   info->math = op->math;
@@ -367,6 +401,7 @@ b2g_status b2g_enqueue_ex(const b2g_op* op, const b2g_enqueue_args* a, b2g_strea
     if (!aligned(a->prefetch_packed, 16)) return B2G_ERR_INVALID;
     p.pf_packed = static_cast<const uint8_t*>(a->prefetch_packed);
     p.pf_total_units = nx->total_units;
+    p.pf_gran = nx->gran;
     p.pf_unit_bytes = nx->unit_bytes;
     p.pf_grid = nx->grid;
     p.pf_bytes = 1 << 30;  // the CTA's whole range

@@ -17,7 +17,9 @@
 //    exist (before the previous kernel is waited on, or before the stack
 //    kernel's grid barrier), since weights are constant.
 //  * The M <= 8 activation rows are staged once per phase in shared memory
-//    with one round of 16 B loads (RMSNorm applied there when fused).  The
+//    with one round of 16 B loads.  RMSNorm is linear in x, so a fused norm
+//    scales the accumulators by each row's factor in the epilogue; the factors
+//    are summed from the staged rows while other warps finish streaming.  The
 //    prepack permutes k inside each block so a lane's B fragment is one 16 B
 //    (E4M3) or 8 B (FP16) shared load; the decode rows fill the n = 8 side of
 //    mma.sync.m16n8k16 (x^T as B).  E4M3 is widened with cvt.rn.f16x2.e4m3x2.
@@ -87,27 +89,22 @@ __device__ __forceinline__ Io io_of_params(const GemvParams& p) {
   return Io{p.packed, p.scales, p.x, p.ldx, p.residual, p.ldr, p.y, p.ldy};
 }
 
-// floor(a / b) for 0 <= a < 2^52 and 0 < b < 2^31, given rb = 1.0 / b
-// rounded to nearest: the double product is within one of the quotient, and
-// one integer correction makes it exact.  (A 64-bit integer division is a
-// long dependent instruction sequence; this is a handful of instructions.)
-__device__ __forceinline__ long long floor_div(long long a, long long b, double rb) {
-  long long q = (long long)((double)a * rb);
-  if (q * b > a)
-    --q;
-  else if ((q + 1) * b <= a)
-    ++q;
-  return q;
+// x / d for 0 <= x < 2^31 with the host-computed constants of d (FastDiv).
+__device__ __forceinline__ int fdiv(int x, const FastDiv& f) {
+  return (int)((__umulhi((uint32_t)x, f.mul) + (uint32_t)x) >> f.shift);
 }
 
-// The CTA whose stream-K range [c*T/G, (c+1)*T/G) holds unit u.
-__device__ __forceinline__ int cta_of(const GemvParams& p, long long u) {
-  return (int)floor_div((u + 1) * p.grid + p.total_units - 1, p.total_units, p.r_units) - 1;
+// The partition: CTA c streams granules [c*Tg/G, (c+1)*Tg/G) of gran units
+// each (Tg = total_gran); cta_of(u) is the CTA whose range holds unit u.
+// All operands stay below 2^31 (host-checked).
+__device__ __forceinline__ int cta_of(const GemvParams& p, int u) {
+  const int gi = fdiv(u, p.div_gran);
+  return fdiv((gi + 1) * p.grid + p.total_gran - 1, p.div_tg) - 1;
 }
 
 // First unit of CTA c's range.
 __device__ __forceinline__ int range_start(const GemvParams& p, int c) {
-  return (int)floor_div((long long)c * p.total_units, p.grid, p.r_grid);
+  return fdiv(c * p.total_gran, p.div_grid) * p.gran;
 }
 
 __device__ __forceinline__ float channel_scale(const GemvParams& p, const Io& io, int plane, int n) {
@@ -129,30 +126,70 @@ __device__ __forceinline__ float2 h2_to_f2(uint32_t v) {
   return __half22float2(h);
 }
 
-__device__ __forceinline__ uint32_t f2_to_h2(float a, float b) {
-  __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
 // Lane layout of a finished tile (the m16n8 accumulator): entry i of lane
 // (g = lane/4, q = lane%4) is channel g + 8*(i/2), token 2q + (i%2).
+// Per-slot epilogue inputs in shared memory, loaded with the activations:
+// the scales of the slot's 16 channels (per plane) and, for a residual op,
+// the residual rows.  Slot j is the CTA's j-th virtual tile.
+struct Epi {
+  float* scale;  // [n_slots][P][16]
+  float* res;    // [n_slots][8][16]
+};
+
+__device__ __forceinline__ Epi epi_of(const GemvParams& p, uint8_t* smem, int P) {
+  float* base = reinterpret_cast<float*>(smem + p.off_epi);
+  return Epi{base, base + p.n_slots * P * 16};
+}
+
 template <int P>
-__device__ void epilogue(const GemvParams& p, const Io& io, int tile, const float (&v)[P][4], int lane) {
+__device__ __forceinline__ void load_epi(const GemvParams& p, const Io& io, const Epi& e, int vt_first, int nvt,
+                                         int tid) {
+  const int ns = nvt * P * 16;
+  for (int i = tid; i < ns; i += NT) {
+    const int j = i / (P * 16), pl = (i / 16) % P, c = i % 16;
+    const int tile = fdiv(vt_first + j, p.div_tiles);
+    const int n = (vt_first + j - tile * p.n_tiles) * kTileCh + c;
+    e.scale[i] = n < p.N ? channel_scale(p, io, pl, n) : 0.f;
+  }
+  if (P == 1 && p.residual_add) {
+    const int nr = nvt * 8 * 16;
+    for (int i = tid; i < nr; i += NT) {
+      const int j = i / 128, m = (i / 16) % 8, c = i % 16;
+      const int vt = vt_first + j;
+      const int n = (vt - fdiv(vt, p.div_tiles) * p.n_tiles) * kTileCh + c;
+      e.res[i] = (m < p.M && n < p.N) ? __half2float(__ldcg(io.residual + (size_t)m * io.ldr + n)) : 0.f;
+    }
+  }
+}
+
+// RMSNorm factor of row m from the partial sums of squares (see rms_partials).
+__device__ __forceinline__ float rms_of(const GemvParams& p, const float* red, int m) {
+  const int parts = W / p.M;
+  float s = 0.f;
+  for (int i = 0; i < parts; ++i) s += red[m * W + i];
+  return 1.0f / sqrtf(s / (float)p.K + p.rms_eps);
+}
+
+// red: RMSNorm partial sums (nullptr when the op has no RMSNorm); the
+// normalisation is linear, so it scales the accumulator: y = fp16(acc * r_m * s_n).
+template <int P>
+__device__ __forceinline__ void epilogue(const GemvParams& p, const Io& io, int j, int tile, const float (&v)[P][4],
+                                         int lane, const float* red, const Epi& e) {
   const int g = lane >> 2, q = lane & 3;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int m = 2 * q + (i & 1);
-    const int n = tile * kTileCh + g + 8 * (i >> 1);
+    const int c = g + 8 * (i >> 1);
+    const int n = tile * kTileCh + c;
     if (m < p.M && n < p.N) {
+      const float r = red ? rms_of(p, red, m) : 1.0f;
       __half out;
       if constexpr (P == 1) {
-        out = __float2half_rn(v[0][i] * channel_scale(p, io, 0, n));
-        if (p.residual_add)
-          out = __float2half_rn(__half2float(__ldcg(io.residual + (size_t)m * io.ldr + n)) +
-                                __half2float(out));
+        out = __float2half_rn(v[0][i] * r * e.scale[j * 16 + c]);
+        if (p.residual_add) out = __float2half_rn(e.res[(j * 8 + m) * 16 + c] + __half2float(out));
       } else {
-        const float gf = __half2float(__float2half_rn(v[0][i] * channel_scale(p, io, 0, n)));
-        const float uf = __half2float(__float2half_rn(v[1][i] * channel_scale(p, io, 1, n)));
+        const float gf = __half2float(__float2half_rn(v[0][i] * r * e.scale[(j * 2) * 16 + c]));
+        const float uf = __half2float(__float2half_rn(v[1][i] * r * e.scale[(j * 2 + 1) * 16 + c]));
         out = __float2half_rn(gf / (1.0f + expf(-gf)) * uf);
       }
       io.y[(size_t)m * io.ldy + n] = out;
@@ -163,83 +200,73 @@ __device__ void epilogue(const GemvParams& p, const Io& io, int tile, const floa
 // A virtual tile's CTA-level sum is complete in v: finish it here if this CTA
 // is the tile's only contributor, else publish it and let the last
 // contributing CTA sum all partials in (k-range, CTA) order.
-constexpr int kMaxKsplit = 8;
 template <int P>
-__device__ __forceinline__ void finish_vt(const GemvParams& p, const Io& io, int vt, const float (&v)[P][4],
-                                          int lane) {
-  // k-ranges whose partials are fetched in one round trip (the rest, and
-  // contributors past the second of a k-range, are read one at a time).
-  constexpr int KU = (P == 1) ? 4 : 2;
-  const int ks = vt / p.n_tiles;
+__device__ __forceinline__ void finish_vt(const GemvParams& p, const Io& io, int vt, int j, const float (&v)[P][4],
+                                          int lane, const float* red, const Epi& e) {
+  const int ks = fdiv(vt, p.div_tiles);
   const int tile = vt - ks * p.n_tiles;
-  int cf[kMaxKsplit], cn[kMaxKsplit];  // first contributing CTA and count per k-range
-  int total = 0, my_first = 0;
-#pragma unroll
-  for (int k = 0; k < kMaxKsplit; ++k) {
-    cf[k] = 0;
-    cn[k] = 0;
-    if (k < p.ksplit) {
-      const long long a = (long long)(k * p.n_tiles + tile) * p.kbpv;
-      cf[k] = cta_of(p, a);
-      cn[k] = cta_of(p, a + p.kbpv - 1) - cf[k] + 1;
-      total += cn[k];
-      if (k == ks) my_first = cf[k];
-    }
-  }
-  if (total == 1) {
-    epilogue<P>(p, io, tile, v, lane);
-    return;
-  }
-  float4* parts = reinterpret_cast<float4*>(p.partials);
-  float4* dst = parts + ((size_t)vt * p.max_contrib + (size_t)(blockIdx.x - my_first)) * P * 32;
-#pragma unroll
-  for (int pl = 0; pl < P; ++pl)
-    __stcg(&dst[pl * 32 + lane], make_float4(v[pl][0], v[pl][1], v[pl][2], v[pl][3]));
-  __syncwarp();
-  int old = 0;
-  if (lane == 0) old = atom_add_acq_rel_gpu(&p.counters[tile], 1);
-  old = __shfl_sync(0xffffffffu, old, 0);
-  if (old != total - 1) return;
-  fence_acq_rel_gpu();
-  auto src = [&](int k, int c) {
-    return parts + ((size_t)(k * p.n_tiles + tile) * p.max_contrib + c) * P * 32 + lane;
+  // Contributors of k-range k: CTAs cta_of(a_k) .. cta_of(a_k + kbpv - 1).
+  auto first_of = [&](int k) { return cta_of(p, (k * p.n_tiles + tile) * p.kbpv); };
+  auto count_of = [&](int k) {
+    const int a = (k * p.n_tiles + tile) * p.kbpv;
+    return cta_of(p, a + p.kbpv - 1) - cta_of(p, a) + 1;
   };
-  float4 t[KU][2][P];
-#pragma unroll
-  for (int k = 0; k < KU; ++k)
-#pragma unroll
-    for (int c = 0; c < 2; ++c)
-#pragma unroll
-      for (int pl = 0; pl < P; ++pl)
-        t[k][c][pl] = (k < p.ksplit && c < cn[k]) ? __ldcg(src(k, c) + pl * 32) : make_float4(0.f, 0.f, 0.f, 0.f);
+  int total = 0;
+#pragma unroll 1
+  for (int k = 0; k < p.ksplit; ++k) total += count_of(k);
   float s[P][4];
 #pragma unroll
-  for (int pl = 0; pl < P; ++pl) s[pl][0] = s[pl][1] = s[pl][2] = s[pl][3] = 0.f;
-  auto add = [&](int pl, const float4& a) {
-    s[pl][0] += a.x;
-    s[pl][1] += a.y;
-    s[pl][2] += a.z;
-    s[pl][3] += a.w;
-  };
+  for (int pl = 0; pl < P; ++pl)
 #pragma unroll
-  for (int k = 0; k < kMaxKsplit; ++k) {
-    if (k >= p.ksplit) break;
-    int c = 0;
-    if (k < KU) {
+    for (int i = 0; i < 4; ++i) s[pl][i] = v[pl][i];
+  if (total > 1) {
+    float4* parts = reinterpret_cast<float4*>(p.partials);
+    auto src = [&](int k, int c) {
+      return parts + ((size_t)(k * p.n_tiles + tile) * p.max_contrib + c) * P * 32 + lane;
+    };
+    float4* dst = src(ks, blockIdx.x - first_of(ks));
 #pragma unroll
-      for (int pl = 0; pl < P; ++pl) {
-        if (cn[k] > 0) add(pl, t[k < KU ? k : 0][0][pl]);
-        if (cn[k] > 1) add(pl, t[k < KU ? k : 0][1][pl]);
+    for (int pl = 0; pl < P; ++pl) __stcg(dst + pl * 32, make_float4(v[pl][0], v[pl][1], v[pl][2], v[pl][3]));
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) old = atom_add_acq_rel_gpu(&p.counters[tile], 1);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old != total - 1) return;
+    fence_acq_rel_gpu();
+    // Last to arrive: sum every partial in (k-range, CTA) order, B per round trip.
+    constexpr int B = (P == 1) ? 8 : 4;
+#pragma unroll
+    for (int pl = 0; pl < P; ++pl) s[pl][0] = s[pl][1] = s[pl][2] = s[pl][3] = 0.f;
+    int k = 0, c = 0, n = count_of(0);
+#pragma unroll 1
+    for (int base = 0; base < total; base += B) {
+      float4 t[B][P];
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const bool have = base + b < total;
+#pragma unroll
+        for (int pl = 0; pl < P; ++pl) t[b][pl] = have ? __ldcg(src(k, c) + pl * 32) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (have && ++c == n) {
+          ++k;
+          c = 0;
+          n = k < p.ksplit ? count_of(k) : 0;
+        }
       }
-      c = 2;
-    }
-    for (; c < cn[k]; ++c) {
 #pragma unroll
-      for (int pl = 0; pl < P; ++pl) add(pl, __ldcg(src(k, c) + pl * 32));
+      for (int b = 0; b < B; ++b)
+        if (base + b < total) {
+#pragma unroll
+          for (int pl = 0; pl < P; ++pl) {
+            s[pl][0] += t[b][pl].x;
+            s[pl][1] += t[b][pl].y;
+            s[pl][2] += t[b][pl].z;
+            s[pl][3] += t[b][pl].w;
+          }
+        }
     }
+    if (lane == 0) p.counters[tile] = 0;
   }
-  if (lane == 0) p.counters[tile] = 0;
-  epilogue<P>(p, io, tile, s, lane);
+  epilogue<P>(p, io, j, tile, s, lane, red, e);
 }
 
 // ---------------------------------------------------------------------------
@@ -250,75 +277,54 @@ __device__ __forceinline__ void finish_vt(const GemvParams& p, const Io& io, int
 // ---------------------------------------------------------------------------
 __device__ void stage_x(const GemvParams& p, const Io& io, __half* xs, int k_lo, int krange, int tid) {
   const int M = p.M, K = p.K;
-  const bool vec = ((reinterpret_cast<uintptr_t>(io.x) & 15) == 0) && ((io.ldx & 7) == 0);
   const int nch = krange / 8;
-  const int total = M * nch;
-  for (int idx = tid; idx < total; idx += NT * 8) {
-    uint4 v[8];
+  const bool vec = ((reinterpret_cast<uintptr_t>(io.x) & 15) == 0) && ((io.ldx & 7) == 0) && k_lo + krange <= K;
+  if (vec) {
+    // Chunk c of every row per thread: up to 8 loads in flight, no index division.
+#pragma unroll 1
+    for (int c = tid; c < nch; c += NT) {
+      uint4 v[8];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const int id = idx + r * NT;
-      v[r] = make_uint4(0, 0, 0, 0);
-      if (id < total) {
-        const int m = id / nch, c = id - m * nch;
-        const int k0 = k_lo + c * 8;
-        const __half* row = io.x + (size_t)m * io.ldx;
-        if (vec && k0 + 8 <= K) {
-          v[r] = __ldcg(reinterpret_cast<const uint4*>(row + k0));
-        } else {
-          uint32_t e[8];
+      for (int m = 0; m < 8; ++m)
+        if (m < M) v[m] = __ldcg(reinterpret_cast<const uint4*>(io.x + (size_t)m * io.ldx + k_lo + c * 8));
 #pragma unroll
-          for (int j = 0; j < 8; ++j) e[j] = (k0 + j < K) ? __half_as_ushort(__ldcg(row + k0 + j)) : 0u;
-          v[r] = make_uint4(e[0] | (e[1] << 16), e[2] | (e[3] << 16), e[4] | (e[5] << 16),
-                            e[6] | (e[7] << 16));
-        }
-      }
+      for (int m = 0; m < 8; ++m)
+        if (m < M) sts128(xs + (size_t)m * p.x_rs + c * 8, v[m]);
     }
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const int id = idx + r * NT;
-      if (id < total) {
-        const int m = id / nch, c = id - m * nch;
-        sts128(xs + (size_t)m * p.x_rs + c * 8, v[r]);
-      }
+  } else {
+    // Unaligned rows or a range past K: element loads, zero past K.
+#pragma unroll 1
+    for (int m = 0; m < M; ++m) {
+      const __half* row = io.x + (size_t)m * io.ldx;
+#pragma unroll 1
+      for (int k = k_lo + tid; k < k_lo + krange; k += NT)
+        xs[(size_t)m * p.x_rs + (k - k_lo)] = k < K ? __ldcg(row + k) : __float2half(0.f);
     }
   }
 }
 
-// In-place RMSNorm of the staged rows (gamma = 1): x <- fp16(x / sqrt(mean(x^2) + eps)).
-// Requires the full row in shared memory (k_lo == 0, K % 8 == 0; host-checked).
-__device__ void rmsnorm_rows(const GemvParams& p, __half* xs, float* rms_r, float* red, int tid) {
-  const int M = p.M, K = p.K;
-  const int nch = K / 8;
-  for (int m = 0; m < M; ++m) {
-    const __half* row = xs + (size_t)m * p.x_rs;
-    float s = 0.f;
-    for (int c = tid; c < nch; c += NT) {
-      const uint4 v = lds128(row + c * 8);
-      const float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), cc = h2_to_f2(v.z), d = h2_to_f2(v.w);
-      s = fmaf(a.x, a.x, s); s = fmaf(a.y, a.y, s); s = fmaf(b.x, b.x, s); s = fmaf(b.y, b.y, s);
-      s = fmaf(cc.x, cc.x, s); s = fmaf(cc.y, cc.y, s); s = fmaf(d.x, d.x, s); s = fmaf(d.y, d.y, s);
-    }
-#pragma unroll
-    for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    if ((tid & 31) == 0) red[(tid >> 5) * 8 + m] = s;
-  }
-  __syncthreads();
-  if (tid < M) {
-    float t = 0.f;
-    for (int w = 0; w < W; ++w) t += red[w * 8 + tid];
-    rms_r[tid] = 1.0f / sqrtf(t / (float)K + p.rms_eps);
-  }
-  __syncthreads();
-  for (int idx = tid; idx < M * nch; idx += NT) {
-    const int m = idx / nch, c = idx - m * nch;
-    __half* at = xs + (size_t)m * p.x_rs + c * 8;
-    const uint4 v = lds128(at);
-    const float r = rms_r[m];
+// Partial sums of squares of the staged rows for RMSNorm (gamma = 1), all
+// warps at once: row m is split over W / M warps, warp part i of row m
+// writing red[m * W + i]; rms_of() adds the parts in order (deterministic).
+// Requires the full row in shared memory (k_lo == 0, zero padding past K).
+__device__ __forceinline__ void rms_partials(const GemvParams& p, const __half* xs, float* red, int warp,
+                                             int lane) {
+  const int parts = W / p.M;
+  const int m = warp / parts, part = warp - m * parts;
+  if (m >= p.M) return;
+  const __half* row = xs + (size_t)m * p.x_rs;
+  const int nch = p.K / 8;
+  float s0 = 0.f, s1 = 0.f;
+  for (int c = part * 32 + lane; c < nch; c += parts * 32) {
+    const uint4 v = lds128(row + c * 8);
     const float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), cc = h2_to_f2(v.z), d = h2_to_f2(v.w);
-    sts128(at, make_uint4(f2_to_h2(a.x * r, a.y * r), f2_to_h2(b.x * r, b.y * r),
-                          f2_to_h2(cc.x * r, cc.y * r), f2_to_h2(d.x * r, d.y * r)));
+    s0 = fmaf(a.x, a.x, s0); s1 = fmaf(a.y, a.y, s1); s0 = fmaf(b.x, b.x, s0); s1 = fmaf(b.y, b.y, s1);
+    s0 = fmaf(cc.x, cc.x, s0); s1 = fmaf(cc.y, cc.y, s1); s0 = fmaf(d.x, d.x, s0); s1 = fmaf(d.y, d.y, s1);
   }
+  float s = s0 + s1;
+#pragma unroll
+  for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) red[m * W + part] = s;
 }
 
 // ---------------------------------------------------------------------------
@@ -466,19 +472,19 @@ __device__ __forceinline__ Range cta_range(const GemvParams& p, int warp) {
   return r;
 }
 
-// Issue the loads of this warp's first D units of a phase.  Every ring entry
-// is written (zero past the warp's units), so the compiler sees the old
-// contents die here and does not keep them live across a phase's combine.
-template <int P, int R>
+// Issue the loads of units [D0, D1) of this warp's first D units of a phase
+// into their ring slots.  Every entry in the range is written (zero past the
+// warp's units), so the compiler sees the old contents die here and does not
+// keep them live across a phase's combine.
+template <int P, int R, int D0 = 0, int D1 = R / P>
 __device__ __forceinline__ void prefetch_phase(const GemvParams& p, const uint8_t* packed,
                                                uint4 (&ring)[R], int warp, int lane, uint64_t pol) {
-  constexpr int D = R / P;
   constexpr int UNIT = P * kUnitPlaneBytes;
   constexpr size_t WSTEP = (size_t)W * UNIT;
   const Range r = cta_range(p, warp);
   const uint8_t* wl = packed + ((size_t)r.u0 + warp) * UNIT + lane * 16;
 #pragma unroll
-  for (int d = 0; d < D; ++d) {
+  for (int d = D0; d < D1; ++d) {
 #pragma unroll
     for (int pl = 0; pl < P; ++pl)
       ring[d * P + pl] = d < r.n_mine ? ldg_stream(wl + d * WSTEP + pl * kUnitPlaneBytes, pol)
@@ -513,8 +519,8 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
   constexpr int UNIT = P * kUnitPlaneBytes;
   constexpr size_t WSTEP = (size_t)W * UNIT;
   constexpr int KPB = (WB == 1) ? 32 : 16;  // k per k-block
-  float* rms_r = reinterpret_cast<float*>(smem + kOffMisc + 16);
-  float* red = reinterpret_cast<float*>(smem + 128);
+  float* red = reinterpret_cast<float*>(smem + kOffRed);  // RMSNorm partial sums [8][W]
+  const Epi epi = epi_of(p, smem, P);
   float4* slots = reinterpret_cast<float4*>(smem + kOffSlots);  // [n_slots][W][P][32]
   __half* xs = reinterpret_cast<__half*>(smem + p.off_x);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -523,20 +529,21 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
   const Range r = cta_range(p, warp);
   const int u0 = r.u0, n_mine = r.n_mine;
   const bool active = r.u1 > r.u0;
-  const int vt_first = u0 / kbpv;
-  const int vt_last = active ? (r.u1 - 1) / kbpv : vt_first - 1;
-  const int k_lo = (vt_first / p.n_tiles) * kbpv * KPB;
-  const int krange = active ? (vt_last / p.n_tiles + 1 - vt_first / p.n_tiles) * kbpv * KPB : 0;
+  const int vt_first = fdiv(u0, p.div_kbpv);
+  const int vt_last = active ? fdiv(r.u1 - 1, p.div_kbpv) : vt_first - 1;
+  const int ks_first = fdiv(vt_first, p.div_tiles);
+  const int k_lo = ks_first * kbpv * KPB;
+  const int krange = active ? (fdiv(vt_last, p.div_tiles) + 1 - ks_first) * kbpv * KPB : 0;
 
   // ---- activations
   if (tid == 0) STRACE(trace_base);
-  if (active) stage_x(p, io, xs, k_lo, krange, tid);
+  if (active) {
+    stage_x(p, io, xs, k_lo, krange, tid);
+    load_epi<P>(p, io, epi, vt_first, vt_last - vt_first + 1, tid);
+  }
   for (int i = tid; i < p.n_slots * W * P * 32; i += NT) slots[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   __syncthreads();
-  if (p.rmsnorm && active) {
-    rmsnorm_rows(p, xs, rms_r, red, tid);
-    __syncthreads();
-  }
+  if (p.rmsnorm && active) rms_partials(p, xs, red, warp, lane);
   if (threadIdx.x == 0) {
     TRACE(2);
     STRACE(trace_base + 1);
@@ -548,7 +555,7 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
   math.zero();
   // Segment bookkeeping: this warp's units in the current virtual tile are
   // counted down; the tile is re-derived only at a segment end.
-  int vt = (u0 + warp) / kbpv;
+  int vt = fdiv(u0 + warp, p.div_kbpv);
   int kbl = (u0 + warp) - vt * kbpv;     // k-block (within vt) of the segment's first unit
   int seg_n = (kbpv - kbl + W - 1) / W;  // this warp's units in vt
   int seg_left = seg_n;
@@ -558,7 +565,7 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
   // row 0: those token columns are computed but never stored.
   const __half* xlane = xs + (size_t)(g < M ? g : 0) * p.x_rs + (WB == 1 ? 8 * q : 4 * q);
   const __half* xq = xs + (WB == 1 ? 8 * q : 4 * q);  // row 0, for the FFMA variant
-  int xoff = ((vt / p.n_tiles) * kbpv + kbl) * KPB - k_lo;  // k offset (halves) of the next unit
+  int xoff = (fdiv(vt, p.div_tiles) * kbpv + kbl) * KPB - k_lo;  // k offset (halves) of the next unit
   uint32_t xa = smem_addr(xlane) + 2 * xoff;                  // its shared address
   const uint8_t* lp = io.packed + ((size_t)u0 + warp) * UNIT + lane * 16 + D * WSTEP;  // unit j0 + D
 
@@ -604,24 +611,18 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
       seg_n = (kbpv - kbl + W - 1) / W;
       seg_left = seg_n;
       cur_j = vt - vt_first;
-      xoff = ((vt / p.n_tiles) * kbpv + kbl) * KPB - k_lo;
+      xoff = (fdiv(vt, p.div_tiles) * kbpv + kbl) * KPB - k_lo;
       xa = smem_addr(xlane) + 2 * xoff;
     }
   };
-  // Whole blocks of D units (slot d of a block refills with unit j0 + D + d
-  // while that exists), then the last partial block, which loads nothing.
-  const int n_full = n_mine - n_mine % D;
-  int j0 = 0;
-  for (; j0 < n_full; j0 += D) {
-    const int lim = n_mine - D - j0;
-#pragma unroll
-    for (int d = 0; d < D; ++d) unit(d, d < lim);
-    lp += (size_t)D * WSTEP;
-  }
-  if (j0 < n_mine) {
+  // Blocks of D units: slot d of a block is used while unit j0 + d exists and
+  // refills with unit j0 + D + d while that exists.
+  for (int j0 = 0; j0 < n_mine; j0 += D) {
+    const int use = n_mine - j0, refill = use - D;
 #pragma unroll
     for (int d = 0; d < D; ++d)
-      if (j0 + d < n_mine) unit(d, false);
+      if (d < use) unit(d, d < refill);
+    lp += (size_t)D * WSTEP;
   }
   if (n_mine > 0 && seg_left != seg_n) flush(cur_j);
   if (threadIdx.x == 0) {
@@ -637,6 +638,7 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
     float v[P][4];
 #pragma unroll
     for (int pl = 0; pl < P; ++pl) v[pl][0] = v[pl][1] = v[pl][2] = v[pl][3] = 0.f;
+#pragma unroll
     for (int w = 0; w < W; ++w) {
 #pragma unroll
       for (int pl = 0; pl < P; ++pl) {
@@ -647,7 +649,7 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
         v[pl][3] += t.w;
       }
     }
-    finish_vt<P>(p, io, vt_first + j, v, lane);
+    finish_vt<P>(p, io, vt_first + j, j, v, lane, p.rmsnorm ? red : nullptr, epi);
   }
 #ifdef B2G_TRACE
   __syncthreads();
@@ -674,8 +676,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_
   // Warm L2 with the range the next kernel's CTA of the same index will
   // stream, so HBM keeps working through this kernel's tail and the launch gap.
   if (tid == 0 && p.pf_packed != nullptr && (int)blockIdx.x < p.pf_grid) {
-    const long long a = (long long)blockIdx.x * p.pf_total_units / p.pf_grid;
-    const long long b = (long long)(blockIdx.x + 1) * p.pf_total_units / p.pf_grid;
+    const long long tg = p.pf_total_units / p.pf_gran;
+    const long long a = (long long)blockIdx.x * tg / p.pf_grid * p.pf_gran;
+    const long long b = (long long)(blockIdx.x + 1) * tg / p.pf_grid * p.pf_gran;
     const long long bytes = min((long long)p.pf_bytes, (b - a) * p.pf_unit_bytes);
     const uint8_t* src = p.pf_packed + a * p.pf_unit_bytes;
     for (long long off = 0; off < bytes; off += 32768)

@@ -22,10 +22,13 @@ constexpr int kTileCh = 16;
 constexpr int kWarps = 16;  // one CTA of 16 warps per SM
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxSlots = 8;  // virtual tiles one CTA may touch
-// Shared memory: [64,68) barrier verdict, [80,112) RMS factors, [128,640)
-// RMSNorm partial sums, then the per-warp partial slots
-// [n_slots][warps][planes][32 lanes][16 B], then the x rows.
+// Shared memory: [64,68) barrier verdict, [128,640) RMSNorm partial sums
+// [8 rows][16 warps], then the per-warp partial slots
+// [n_slots][warps][planes][32 lanes][16 B], then the per-slot epilogue inputs
+// (scales [n_slots][planes][16], residual rows [n_slots][8][16], fp32), then
+// the x rows.
 constexpr int kOffMisc = 64;
+constexpr int kOffRed = 128;
 constexpr int kOffSlots = 1024;
 // Workspace: tile counters first (fixed size, so ops sharing one workspace
 // agree on where they are), then the split-K partials.  The last 256 bytes of
@@ -35,6 +38,21 @@ constexpr int kBarrierWordOffset = kCounterRegionBytes - 256;
 constexpr int kMaxTiles = kBarrierWordOffset / 4;
 
 enum MathKind : int { kMathMma = 0, kMathFfma = 1 };
+
+// Division of x < 2^31 by a divisor fixed per launch, as a multiply-high and
+// a shift (Granlund & Montgomery, "Division by invariant integers using
+// multiplication", 1994, fig. 4.1 with N = 32):
+//   l = ceil(log2 d), mul = floor(2^32 (2^l - d) / d) + 1,
+//   x / d = (umulhi(x, mul) + x) >> l   (the sum stays below 2^32 for x < 2^31).
+struct FastDiv {
+  uint32_t d, mul, shift;
+};
+inline FastDiv make_fast_div(uint32_t d) {
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;
+  const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
+  return FastDiv{d, (uint32_t)m, l};
+}
 
 struct GemvParams {
   const uint8_t* packed;
@@ -49,26 +67,33 @@ struct GemvParams {
   int* counters;    // [n_tiles], zero between calls
   int* error;
   long long total_units;
-  double r_units;  // 1.0 / total_units and 1.0 / grid (exact floor divisions, see floor_div)
-  double r_grid;
+  // Partition: the stream is cut into `grid` ranges at granules of `gran`
+  // units (1: stream-K, any unit; kbpv: whole virtual tiles).
+  int gran;
+  FastDiv div_gran;
+  int total_gran;  // total_units / gran; (total_gran + 2) * grid < 2^31 (host-checked)
+  FastDiv div_tg, div_grid;
   int grid;
   int n_tiles;
   int kb_total;  // k-blocks (32 k for E4M3, 16 k for FP16) over padded K
   int ksplit;
   int kbpv;  // k-blocks per virtual tile
+  FastDiv div_kbpv, div_tiles;  // / kbpv and / n_tiles
   int M, K, N;
   int scale_mode;
-  int rmsnorm;
+  int rmsnorm;  // rows are RMS-normalised: the factor is applied to the accumulators
   int residual_add;
   float rms_eps;
   int max_contrib;
   int n_slots;    // max virtual tiles per CTA (<= kMaxSlots)
+  int off_epi;    // shared-memory byte offset of the epilogue inputs
   int off_x;      // shared-memory byte offset of the x rows
   int x_rs;       // x row stride in shared memory (halves)
   // L2 prefetch of the next kernel's stream: CTA c prefetches the first
   // pf_bytes of the range the next kernel's CTA c will stream (0 = off).
   const uint8_t* pf_packed;
   long long pf_total_units;
+  int pf_gran;
   int pf_unit_bytes;
   int pf_grid;
   int pf_bytes;

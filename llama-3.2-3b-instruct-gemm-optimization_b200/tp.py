@@ -1,0 +1,117 @@
+"""Tensor-parallel decode-MLP stack: one process (one GPU) per rank.
+
+The layer shards the way the MLP's algebra allows (no reference counterpart:
+the reference runs on one GPU):
+
+* gate and up are split by output columns: rank r owns intermediate channels
+  [r*I/tp, (r+1)*I/tp) of both and computes its slice of act = SiLU(g)*u with
+  no communication (SiLU*up is elementwise per channel);
+* down is split by K over the same channel range, so each rank multiplies its
+  own act slice and produces a full-width [M, hidden] fp16 partial;
+* one all-reduce (sum) of the partials per layer; rank 0's down adds the
+  residual in its epilogue and the others write a bare partial, so the sum is
+  h + down(act) with the residual counted once.
+
+RMSNorm runs replicated (each rank normalises the same h).  The GEMVs run in
+the C-ABI library (``GemvOp``); torch.distributed (NCCL on GPUs) carries the
+all-reduce.
+"""
+from __future__ import annotations
+
+from . import FUSE_GATE_UP_SILU, FUSE_NONE, FUSE_RESIDUAL_ADD, FUSE_RMSNORM_INPUT, GemvOp
+
+
+def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
+    """[lo, hi) of rank's equal share of n channels (n must divide evenly)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of {world}")
+    if n % world:
+        raise ValueError(f"{n} channels do not split evenly over {world} ranks")
+    step = n // world
+    return rank * step, (rank + 1) * step
+
+
+class TPStack:
+    """n_layers x [RMSNorm -> gate||up + SiLU*up -> down + residual], sharded
+    over the ranks of ``group`` (default: the world group)."""
+
+    def __init__(self, hidden: int = 3072, intermediate: int = 8192, n_layers: int = 28,
+                 rank: int = 0, world: int = 1, weight_dtype="fp8_e4m3", scale_mode="channel_fp32",
+                 max_m: int = 8, rms_eps: float = 1e-5, group=None, build_ops: bool = True):
+        self.hidden, self.intermediate, self.n_layers = hidden, intermediate, n_layers
+        self.rank, self.world, self.group = rank, world, group
+        self.lo, self.hi = shard_range(intermediate, rank, world)
+        self.shard = self.hi - self.lo
+        self.max_m, self.rms_eps = max_m, rms_eps
+        self.layers = [None] * n_layers
+        self.gate_up = self.down = None
+        if build_ops:
+            kw = dict(weight_dtype=weight_dtype, scale_mode=scale_mode, max_m=max_m,
+                      tp_rank=rank, tp_size=world)
+            self.gate_up = GemvOp(hidden, self.shard, fuse=FUSE_GATE_UP_SILU | FUSE_RMSNORM_INPUT, **kw)
+            self.down = GemvOp(self.shard, hidden,
+                               fuse=FUSE_RESIDUAL_ADD if rank == 0 else FUSE_NONE, **kw)
+
+    # -- weights -------------------------------------------------------------
+    def slice_layer(self, wg, wu, wd, sg=None, su=None, sd=None):
+        """This rank's shard of full [K, N] layer weights and per-channel scales:
+        gate/up columns and their scales, down rows (K); down's scales are per
+        output channel and stay whole."""
+        cs = slice(self.lo, self.hi)
+
+        def cols(s):
+            return None if s is None else s[cs]
+        return wg[:, cs], wu[:, cs], wd[cs, :], cols(sg), cols(su), sd
+
+    def set_layer(self, layer: int, packed_gu, scales_gu, packed_d, scales_d):
+        self.layers[layer] = (packed_gu, scales_gu, packed_d, scales_d)
+
+    def prepack_layer(self, layer: int, wg, wu, wd, sg=None, su=None, sd=None):
+        """Slice full device weights for this rank, prepack and register them."""
+        import torch
+        g, u, d, sg_, su_, sd_ = self.slice_layer(wg, wu, wd, sg, su, sd)
+        pgu = self.gate_up.prepack(g.contiguous(), u.contiguous())
+        pd = self.down.prepack(d.contiguous())
+        sgu = None if sg_ is None else torch.cat([sg_, su_]).contiguous()
+        self.set_layer(layer, pgu, sgu, pd, sd_)
+
+    def workspace(self, device="cuda"):
+        import torch
+        n = max(self.gate_up.workspace_bytes(), self.down.workspace_bytes())
+        return torch.zeros(n, dtype=torch.uint8, device=device)
+
+    # -- one layer -----------------------------------------------------------
+    def gate_up_step(self, layer: int, h, act, workspace):
+        """act[:, shard] = SiLU(RMSNorm(h) . Wg_shard) * (RMSNorm(h) . Wu_shard);
+        L2 meanwhile fetches the start of this layer's down shard."""
+        pgu, sgu, pd, _ = self.layers[layer]
+        self.gate_up.enqueue(h, pgu, sgu, y=act, workspace=workspace, rms_eps=self.rms_eps, pdl=True,
+                             prefetch=(self.down, pd))
+
+    def down_step(self, layer: int, act, h, workspace):
+        """h <- h + act . Wd_shard on rank 0, h <- act . Wd_shard elsewhere;
+        L2 meanwhile fetches the start of the next layer's gate||up shard."""
+        _, _, pd, sd = self.layers[layer]
+        nxt = self.layers[(layer + 1) % self.n_layers]
+        self.down.enqueue(act, pd, sd, y=h, residual=h if self.rank == 0 else None,
+                          workspace=workspace, pdl=True,
+                          prefetch=None if nxt is None else (self.gate_up, nxt[0]))
+
+    def reduce_step(self, h):
+        """Sum the ranks' [M, hidden] partials in place (h on every rank)."""
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(h, group=self.group)
+
+    def layer_step(self, layer: int, h, act, workspace):
+        if self.layers[layer] is None:
+            raise RuntimeError(f"layer {layer} has no weights")
+        self.gate_up_step(layer, h, act, workspace)
+        self.down_step(layer, act, h, workspace)
+        self.reduce_step(h)
+
+    def enqueue(self, h, act, workspace):
+        """All layers on h [M, hidden] fp16 in place; act is [M, I/tp] scratch."""
+        for layer in range(self.n_layers):
+            self.layer_step(layer, h, act, workspace)
+        return h

@@ -154,6 +154,30 @@ def test_grid_partitions(b2g, orc, syn, cuda, K, N, grid):
     check(orc, y, orc.gemv(Wh, orc.WTYPE_FP8, x, 3, s), 1, grid)
 
 
+@pytest.mark.parametrize("part", ["units", "tiles"])
+@pytest.mark.parametrize("K,N,fuse,grid", [(3072, 8192, 0, 0), (8192, 3072, 0, 0), (200, 120, 0, 0),
+                                           (3072, 8192, 3, 0), (8192, 3072, 0, 120), (1000, 40, 0, 0)])
+def test_partition_modes(b2g, orc, syn, cuda, part, K, N, fuse, grid):
+    """Equal byte ranges (tiles split between CTAs) and whole tiles per CTA."""
+    mode = {"units": b2g.PARTITION_UNITS, "tiles": b2g.PARTITION_TILES}[part]
+    Wd, Wh, s = make_weights(orc, syn, 35, K, N, 1, 3)
+    w1 = None
+    if fuse & b2g.FUSE_GATE_UP_SILU:
+        Wd1, Wh1, s1 = make_weights(orc, syn, 36, K, N, 1, 3)
+        w1, s = Wd1, np.concatenate([s, s1])
+    for M in (1, 8):
+        x = syn.activations(11 + M, M, K)
+        op, _, y = run_op(b2g, K, N, 1, 3, dev(x), Wd, s, fuse=fuse, w1=w1,
+                          options={b2g.OPT_PARTITION: mode, b2g.OPT_GRID: grid})
+        assert op.plan(M)["partition"] == mode
+        if fuse & b2g.FUSE_GATE_UP_SILU:
+            want = orc.gate_up_silu(orc.rmsnorm(x), Wh, Wh1, orc.WTYPE_FP8, 3, s[:N], s[N:])
+        else:
+            want = orc.gemv(Wh, orc.WTYPE_FP8, x, 3, s)
+        check(orc, y, np.asarray(want, np.float64), 1, (part, M))
+    assert b2g.device_error() == 0
+
+
 def test_deterministic_and_rows_independent(b2g, orc, syn, cuda):
     K, N = 3072, 8192
     Wd, Wh, s = make_weights(orc, syn, 35, K, N, 1, 3)

@@ -111,9 +111,11 @@ def test_static_rejects_oversize_and_workspace(b2g, cuda):
     ERR_SCRATCH_LIMIT before anything is launched; a caller workspace is
     refused (that is b2g_enqueue_ex's job)."""
     import ctypes
-    # 4096 CTAs on gate||up: up to 8 CTAs share a tile, 4.1 MiB of partials.
+    # 4096 CTAs on gate||up cut into equal byte ranges: up to 8 CTAs share a
+    # tile, 4.1 MiB of partials.
     big = b2g.GemvOp(3072, 8192, weight_dtype="fp8_e4m3", scale_mode="none", max_m=8,
                      fuse=b2g.FUSE_GATE_UP_SILU)
+    big.set_option(b2g.OPT_PARTITION, b2g.PARTITION_UNITS)
     big.set_option(b2g.OPT_GRID, 4096)
     assert big.workspace_bytes() > b2g.STATIC_SCRATCH_BYTES
     x = torch.zeros((1, 3072), dtype=torch.float16, device="cuda")
