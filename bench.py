@@ -321,7 +321,7 @@ def run_ours(args):
         st.enqueue(h, act, ws)
 
     step = step_stack if st is not None else step_ops
-    launches_per_step = (LAYERS + 31) // 32 if st is not None else 2 * LAYERS
+    launches_per_step = 2 * LAYERS  # the stack's default per-layer mode and the TP path
 
     # CUDA graph of one step (the serving path); direct launches as a fallback
     graph = None
@@ -376,31 +376,20 @@ def run_ours(args):
     reps = max(5, args.steps // 20)
     detail_extra = {}
     if st is not None:
-        # The per-layer launch path of the same stack, for comparison.
-        st.set_mode("per_layer")
+        # The stack's other execution mode (one persistent cooperative launch
+        # per step), for comparison.
+        st.set_mode("persistent")
         for _ in range(3):
             step_stack()
         ms_pl = timed(step_stack, reps) / reps
-        st.set_mode("persistent")
-        detail_extra["per_layer_launches_ms_per_step"] = round(ms_pl, 5)
-        detail_extra["per_layer_launches_us_per_layer"] = round(ms_pl * 1e3 / LAYERS, 3)
+        st.set_mode("per_layer")
+        detail_extra["persistent_kernel_ms_per_step"] = round(ms_pl, 5)
+        detail_extra["persistent_kernel_us_per_layer"] = round(ms_pl * 1e3 / LAYERS, 3)
 
-    # ---- dominant kernel.  One GPU: the stack kernel is the step's only
-    # launch, so its duration is the graph replay time per step.
-    if st is not None:
-        achieved = bytes_rank / (ms_step * 1e-3) / 1e9
-        traffic = None
-        tf = ROOT / "profiles" / "traffic.json"
-        if tf.exists():
-            traffic = json.loads(tf.read_text()).get(f"stack_m{M}")
-        roofline = {"kernel": "stack_kernel<1> (28 layers: RMSNorm + gate||up + SiLU*up, down + residual)",
-                    "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                    "frac": round(achieved / hbm, 4), "traffic": traffic,
-                    "peak_source": f"{peak_kind} hbm_gbs (STREAM-style copy)",
-                    "alg_bytes_per_launch": bytes_rank,
-                    "us_per_launch": round(ms_step * 1e3, 3)}
-
-    # ---- per-op kernels: fused RMSNorm + gate||up + SiLU*up, 28 layers back to back
+    # ---- dominant kernel: the fused RMSNorm + gate||up + SiLU*up GEMV (two
+    # thirds of the bytes), its 28 layers back to back exactly as the step
+    # chains them (PDL, L2 prefetch of the next launch); CUDA events on the
+    # launching stream.
     def gu_sweep():
         for i, L in enumerate(layers):
             gu_op.enqueue(h, L["pgu"], L["sgu"], y=act, workspace=ws, pdl=True,
@@ -408,17 +397,16 @@ def run_ours(args):
     for _ in range(3):
         gu_sweep()
     ms_gu = timed(gu_sweep, reps) / (reps * LAYERS)
-    if st is None:
-        achieved = gu_b / (ms_gu * 1e-3) / 1e9
-        traffic = None
-        tf = ROOT / "profiles" / "traffic.json"
-        if tf.exists():
-            traffic = json.loads(tf.read_text()).get(f"gate_up_m{M}_tp{tp}")
-        roofline = {"kernel": "gemv_streamk_kernel<2,1,0> (RMSNorm + gate||up + SiLU*up)",
-                    "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                    "frac": round(achieved / hbm, 4), "traffic": traffic,
-                    "peak_source": f"{peak_kind} hbm_gbs (STREAM-style copy)",
-                    "alg_bytes_per_launch": gu_b, "us_per_launch": round(ms_gu * 1e3, 3)}
+    achieved = gu_b / (ms_gu * 1e-3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(f"gate_up_m{M}_tp{tp}")
+    roofline = {"kernel": "gemv_streamk_kernel<2,1,0> (RMSNorm + gate||up + SiLU*up)",
+                "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4), "traffic": traffic,
+                "peak_source": f"{peak_kind} hbm_gbs (STREAM-style copy)",
+                "alg_bytes_per_launch": gu_b, "us_per_launch": round(ms_gu * 1e3, 3)}
 
     def dn_sweep():
         for i, L in enumerate(layers):
@@ -462,12 +450,13 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None, "dtype": "fp8_e4m3", "data": "synthetic",
             "config": {
-                "workload": (f"28-layer Llama-3.2-3B decode MLP stack, M={M}: RMSNorm(eps 1e-5) -> "
+                "workload": (f"{LAYERS}-layer Llama-3.2-3B decode MLP stack, M={M}: RMSNorm(eps 1e-5) -> "
                              f"fused gate||up 3072->2x8192 + SiLU*up -> down 8192->3072 + residual; "
                              f"E4M3 weights, per-channel FP32 scales, fp16 activations, fp32 accumulate"),
                 "hidden": HIDDEN, "intermediate": INTER, "layers": LAYERS, "m": M,
                 "parallelism": f"tp{tp}", "weights_per_step_bytes": bytes_rank * tp,
-                "l2": "inputs larger than L2: 2.12 GB of weights streamed per step (L2 126 MB), no flush",
+                "l2": (f"inputs larger than L2: {bytes_rank * tp / 1e9:.2f} GB of weights streamed per step "
+                       "(L2 126 MB), no flush"),
                 "timing": "CUDA graph replay of one step" if graph is not None else "direct launches",
                 "data": "N(0,0.02) weights and N(0,1) hidden state from seeded device RNG",
             },
@@ -499,8 +488,13 @@ def run_ours(args):
         if graph is None:
             line["detail"]["graph_error"] = graph_error
         print(json.dumps(line), flush=True)
+    # Release the captured graph (it holds NCCL work when tp > 1) before the
+    # process group goes: `run` is a bound method that keeps it alive.
+    torch.cuda.synchronize()
+    run = None
     if graph is not None:
-        del graph
+        graph.reset()
+        graph = None
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -532,7 +526,7 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": us_layer * LAYERS / 1e3,
         "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
         "dtype": "fp8_e4m3", "data": "synthetic",
-        "config": {"workload": (f"28-layer Llama-3.2-3B decode MLP stack, M={args.m} (CPU sample: "
+        "config": {"workload": (f"{LAYERS}-layer Llama-3.2-3B decode MLP stack, M={args.m} (CPU sample: "
                                 f"layer 0's three E4M3 GEMVs, scaled to the stack)"),
                    "hidden": HIDDEN, "intermediate": INTER, "layers": LAYERS, "m": args.m,
                    "parallelism": "host cores"},
@@ -553,7 +547,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ref-kernels", action="store_true", help="skip timing the reference's GPU kernels")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="decode-MLP layers (28 = Llama-3.2-3B; fewer only for small profiling captures)")
     args = ap.parse_args()
+    globals()["LAYERS"] = args.layers
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

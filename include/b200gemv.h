@@ -258,12 +258,14 @@ b2g_status b2g_stack_set_layer(b2g_stack* st, int32_t layer, const void* packed_
 b2g_status b2g_stack_workspace_size(const b2g_stack* st, int32_t m, size_t* bytes);
 b2g_status b2g_stack_workspace_init(const b2g_stack* st, void* workspace, b2g_stream_t stream);
 /* Execution mode (key B2G_STACK_OPT_MODE):
- *  PERSISTENT (default): one cooperative launch runs every layer (up to 32
- *    layers per launch), grid barriers between the gate||up and down phases;
- *    each phase's first weights are loaded while the barrier completes.
- *  PER_LAYER: two launches per layer chained with programmatic dependent
- *    launch and an L2 prefetch of the next launch's first weights.
- * Both give bitwise-identical results. */
+ *  PER_LAYER (default): two launches per layer chained with programmatic
+ *    dependent launch; each launch first loads its own leading weights, then
+ *    asks L2 for the next launch's whole range.
+ *  PERSISTENT: one cooperative launch runs every layer (up to 32 layers per
+ *    launch), grid barriers between the gate||up and down phases; each
+ *    phase's first weights are loaded while the barrier completes.
+ * Both give bitwise-identical results; on B200 PER_LAYER is currently the
+ * faster of the two (see the benchmark's detail output). */
 enum { B2G_STACK_OPT_MODE = 1 };
 enum { B2G_STACK_MODE_PERSISTENT = 0, B2G_STACK_MODE_PER_LAYER = 1 };
 b2g_status b2g_stack_set_option(b2g_stack* st, int32_t key, int32_t value);

@@ -508,6 +508,7 @@ b2g_status b2g_stack_create(const b2g_stack_fields* f, b2g_stack** out) {
   auto* st = new (std::nothrow) b2g_stack();
   if (!st) return B2G_ERR_OOM;
   st->f = *f;
+  st->mode = B2G_STACK_MODE_PER_LAYER;
   b2g_status s = b2g_create(&g, &st->gu);
   if (s == B2G_OK) s = b2g_create(&d, &st->dn);
   if (s != B2G_OK) {

@@ -84,7 +84,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 
 // ---------------------------------------------------------------------------
 // 1-D bulk copy global -> shared (TMA), completion counted on an mbarrier.
-// src/dst 16-byte aligned, bytes a multiple of 16.  No multicast.
+// src/dst 16-byte aligned, bytes a multiple of 16; this CTA's shared memory only.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t pol;
