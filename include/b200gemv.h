@@ -140,8 +140,10 @@ b2g_status b2g_destroy(b2g_op* op);
  *    UNITS = equal byte ranges (a 16-channel tile may be split between two
  *    CTAs, which then combine partial sums); TILES = whole tiles per CTA (no
  *    split, up to one tile of imbalance); AUTO (default) = TILES when K is
- *    not split and the imbalance is at most 20%, else UNITS. */
-enum { B2G_OPT_MATH = 1, B2G_OPT_GRID = 2, B2G_OPT_PARTITION = 3 };
+ *    not split and the imbalance is at most 20%, else UNITS.
+ *  B2G_OPT_KSPLIT: number of K ranges (0 = automatic).  Changes the packed
+ *    layout: set it before b2g_prepack. */
+enum { B2G_OPT_MATH = 1, B2G_OPT_GRID = 2, B2G_OPT_PARTITION = 3, B2G_OPT_KSPLIT = 4 };
 enum { B2G_PARTITION_AUTO = 0, B2G_PARTITION_UNITS = 1, B2G_PARTITION_TILES = 2 };
 b2g_status b2g_op_set_option(b2g_op* op, int32_t key, int32_t value);
 

@@ -25,7 +25,7 @@ DTYPE = {"fp16": 0, "fp8_e4m3": 1}
 SCALE = {"none": 0, "tensor_fp16": 1, "channel_fp16": 2, "channel_fp32": 3}
 LAYOUT = {"KN": 0, "NK": 1}
 FUSE_NONE, FUSE_GATE_UP_SILU, FUSE_RMSNORM_INPUT, FUSE_RESIDUAL_ADD = 0, 1, 2, 4
-OPT_MATH, OPT_GRID, OPT_PARTITION = 1, 2, 3
+OPT_MATH, OPT_GRID, OPT_PARTITION, OPT_KSPLIT = 1, 2, 3, 4
 PARTITION_AUTO, PARTITION_UNITS, PARTITION_TILES = 0, 1, 2
 MATH_MMA, MATH_FFMA = 0, 1
 STACK_OPT_MODE = 1

@@ -27,7 +27,7 @@ struct b2g_op {
   int unit_bytes;
   size_t packed_bytes;
   int device, num_sms, smem_optin, smem_per_sm;
-  int grid, grid_override;
+  int grid, grid_override, ksplit_override;
   int partition, gran;  // B2G_PARTITION_* requested; units per granule in use
   long long total_gran;
   int max_contrib, n_slots, xk_cap;
@@ -66,6 +66,24 @@ b2g_status ensure_device_setup(int dev, int smem_optin) {
     g_limit_set[dev] = true;
   }
   return B2G_OK;
+}
+
+// K ranges: `want` if it is valid (0 = automatic).  Automatic keeps K whole
+// while max_m activation rows fit in 128 KB of shared memory (whole rows cost
+// one staging copy but need no cross-range reduction; measured faster on
+// B200), else the largest of 8/4/2 that leaves each range >= 2048 k.  A range
+// must hold whole k-blocks and a multiple of 32 k; RMSNorm needs whole rows in
+// one CTA, so no split.
+int choose_ksplit(const b2g_op* op, int want) {
+  auto ok = [&](int ks) {
+    return ks >= 1 && op->kb_total % ks == 0 && ((op->kb_total / ks) * op->kpb) % 32 == 0;
+  };
+  if (op->f.fuse & B2G_FUSE_RMSNORM_INPUT) return want <= 1 ? 1 : -1;
+  if (want > 0) return ok(want) ? want : -1;
+  if ((long long)op->f.max_m * op->Kp * 2 <= 128 * 1024) return 1;
+  for (int ks : {8, 4, 2})
+    if (op->K / ks >= 2048 && ok(ks)) return ks;
+  return 1;
 }
 
 // The partition (mirrors cta_of / range_start in gemv.cu): CTA c streams
@@ -136,6 +154,12 @@ b2g_status replan(b2g_op* op) {
   op->gran = aligned ? op->kbpv : 1;
   op->total_gran = op->total_units / op->gran;
   op->grid = (int)std::min<long long>(op->total_gran, want);
+  if (aligned) {
+    // The fewest CTAs that keep the same largest share of tiles: no CTA
+    // waits on another that holds one tile more.
+    const long long per = (op->total_gran + op->grid - 1) / op->grid;
+    op->grid = (int)((op->total_gran + per - 1) / per);
+  }
   // The kernels' partition arithmetic is 32-bit.
   if ((op->total_gran + 2) * (long long)op->grid >= (1LL << 31)) return B2G_ERR_UNSUPPORTED;
   plan_partition(op);
@@ -223,7 +247,6 @@ b2g_status b2g_create(const b2g_fields* f, b2g_op** out) {
   op->Kp = (op->K + 31) / 32 * 32;
   op->kb_total = op->Kp / op->kpb;
   op->n_tiles = (op->N + kTileCh - 1) / kTileCh;
-  op->ksplit = 1;
   if (op->n_tiles > kMaxTiles) {
     delete op;
     return B2G_ERR_UNSUPPORTED;
@@ -232,14 +255,7 @@ b2g_status b2g_create(const b2g_fields* f, b2g_op** out) {
     delete op;
     return B2G_ERR_UNSUPPORTED;
   }
-  // RMSNorm needs whole rows in one CTA: no K split.
-  for (int ks : {8, 4, 2}) {
-    if (f->fuse & B2G_FUSE_RMSNORM_INPUT) break;
-    if (op->K / ks >= 2048 && op->kb_total % ks == 0 && ((op->kb_total / ks) * op->kpb) % 32 == 0) {
-      op->ksplit = ks;
-      break;
-    }
-  }
+  op->ksplit = choose_ksplit(op, 0);
   op->kbpv = op->kb_total / op->ksplit;
   op->total_units = (long long)op->n_tiles * op->kb_total;
   if (op->total_units >= (1LL << 30)) {
@@ -274,8 +290,18 @@ b2g_status b2g_destroy(b2g_op* op) {
   return B2G_OK;
 }
 
+static b2g_status set_option_unchecked(b2g_op* op, int32_t key, int32_t value);
+
+// An option that leaves no valid plan is refused and the op keeps its plan.
 b2g_status b2g_op_set_option(b2g_op* op, int32_t key, int32_t value) {
   if (!op) return B2G_ERR_INVALID;
+  const b2g_op saved = *op;
+  const b2g_status st = set_option_unchecked(op, key, value);
+  if (st != B2G_OK) *op = saved;
+  return st;
+}
+
+static b2g_status set_option_unchecked(b2g_op* op, int32_t key, int32_t value) {
   switch (key) {
     case B2G_OPT_MATH:
       if (value != kMathMma && value != kMathFfma) return B2G_ERR_INVALID;
@@ -289,6 +315,14 @@ b2g_status b2g_op_set_option(b2g_op* op, int32_t key, int32_t value) {
       if (value < B2G_PARTITION_AUTO || value > B2G_PARTITION_TILES) return B2G_ERR_INVALID;
       op->partition = value;
       return replan(op);
+    case B2G_OPT_KSPLIT: {
+      const int ks = choose_ksplit(op, value);
+      if (value < 0 || ks < 1) return B2G_ERR_INVALID;
+      op->ksplit_override = value;
+      op->ksplit = ks;
+      op->kbpv = op->kb_total / ks;
+      return replan(op);
+    }
   }
   return B2G_ERR_INVALID;
 }
@@ -575,7 +609,8 @@ static b2g_status stack_enqueue_persistent(const b2g_stack* st, int32_t m, void*
                                            cudaStream_t stream) {
   const b2g_op* gu = st->gu;
   const b2g_op* dn = st->dn;
-  if (gu->grid != dn->grid || gu->wbytes != dn->wbytes) return B2G_ERR_UNSUPPORTED;
+  if (gu->wbytes != dn->wbytes) return B2G_ERR_UNSUPPORTED;
+  const int grid = std::max(gu->grid, dn->grid);
   if (!aligned(ws, 16) || !aligned(h, 2) || !aligned(act, 2)) return B2G_ERR_INVALID;
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess) return B2G_ERR_CUDA;
@@ -587,7 +622,7 @@ static b2g_status stack_enqueue_persistent(const b2g_stack* st, int32_t m, void*
   const size_t smem = std::max(lg.smem, ld.smem);
   int max_grid = 0;
   if (stack_max_coresident(gu->wbytes, smem, gu->num_sms, &max_grid) != cudaSuccess) return B2G_ERR_CUDA;
-  if (gu->grid > max_grid) return B2G_ERR_UNSUPPORTED;
+  if (grid > max_grid) return B2G_ERR_UNSUPPORTED;
   StackParams sp = {};
   fill_plan(gu, m, lg, ws, dev, &sp.gu);
   fill_plan(dn, m, ld, ws, dev, &sp.dn);
@@ -604,7 +639,7 @@ static b2g_status stack_enqueue_persistent(const b2g_stack* st, int32_t m, void*
       sp.layers[i] = StackLayer{static_cast<const uint8_t*>(L.pgu), L.sgu, static_cast<const uint8_t*>(L.pd),
                                 L.sd};
     }
-    if (launch_stack(sp, gu->wbytes, smem, stream) != cudaSuccess) return B2G_ERR_CUDA;
+    if (launch_stack(sp, grid, gu->wbytes, smem, stream) != cudaSuccess) return B2G_ERR_CUDA;
   }
   return B2G_OK;
 }

@@ -162,12 +162,12 @@ __device__ __forceinline__ void load_epi(const GemvParams& p, const Io& io, cons
   }
 }
 
-// RMSNorm factor of row m from the partial sums of squares (see rms_partials).
+// RMSNorm factor of row m from the per-warp sums of squares (see stage_x).
 __device__ __forceinline__ float rms_of(const GemvParams& p, const float* red, int m) {
-  const int parts = W / p.M;
   float s = 0.f;
-  for (int i = 0; i < parts; ++i) s += red[m * W + i];
-  return 1.0f / sqrtf(s / (float)p.K + p.rms_eps);
+#pragma unroll
+  for (int w = 0; w < W; ++w) s += red[w * 8 + m];
+  return rsqrtf(s / (float)p.K + p.rms_eps);
 }
 
 // red: RMSNorm partial sums (nullptr when the op has no RMSNorm); the
@@ -176,13 +176,16 @@ template <int P>
 __device__ __forceinline__ void epilogue(const GemvParams& p, const Io& io, int j, int tile, const float (&v)[P][4],
                                          int lane, const float* red, const Epi& e) {
   const int g = lane >> 2, q = lane & 3;
+  // this lane's two token rows, 2q and 2q + 1
+  const float r0 = (red && 2 * q < p.M) ? rms_of(p, red, 2 * q) : 1.0f;
+  const float r1 = (red && 2 * q + 1 < p.M) ? rms_of(p, red, 2 * q + 1) : 1.0f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int m = 2 * q + (i & 1);
     const int c = g + 8 * (i >> 1);
     const int n = tile * kTileCh + c;
     if (m < p.M && n < p.N) {
-      const float r = red ? rms_of(p, red, m) : 1.0f;
+      const float r = (i & 1) ? r1 : r0;
       __half out;
       if constexpr (P == 1) {
         out = __float2half_rn(v[0][i] * r * e.scale[j * 16 + c]);
@@ -190,7 +193,7 @@ __device__ __forceinline__ void epilogue(const GemvParams& p, const Io& io, int 
       } else {
         const float gf = __half2float(__float2half_rn(v[0][i] * r * e.scale[(j * 2) * 16 + c]));
         const float uf = __half2float(__float2half_rn(v[1][i] * r * e.scale[(j * 2 + 1) * 16 + c]));
-        out = __float2half_rn(gf / (1.0f + expf(-gf)) * uf);
+        out = __float2half_rn(gf / (1.0f + __expf(-gf)) * uf);
       }
       io.y[(size_t)m * io.ldy + n] = out;
     }
@@ -275,10 +278,18 @@ __device__ __forceinline__ void finish_vt(const GemvParams& p, const Io& io, int
 // up to 8 each in flight (M = 8 rows of 3072 halves is one round).  L2 loads
 // (ld.cg): x may have been written by another CTA of the same launch.
 // ---------------------------------------------------------------------------
-__device__ void stage_x(const GemvParams& p, const Io& io, __half* xs, int k_lo, int krange, int tid) {
+// With `red` non-null (RMSNorm ops, whole rows staged) the loaded values also
+// give each row's sum of squares: every thread sums its own chunks, each warp
+// reduces across its lanes and writes red[warp * 8 + m]; rms_of() adds the
+// warps in order (deterministic).
+__device__ void stage_x(const GemvParams& p, const Io& io, __half* xs, int k_lo, int krange, int tid,
+                        float* red) {
   const int M = p.M, K = p.K;
   const int nch = krange / 8;
   const bool vec = ((reinterpret_cast<uintptr_t>(io.x) & 15) == 0) && ((io.ldx & 7) == 0) && k_lo + krange <= K;
+  float ss[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) ss[m] = 0.f;
   if (vec) {
     // Chunk c of every row per thread: up to 8 loads in flight, no index division.
 #pragma unroll 1
@@ -289,42 +300,46 @@ __device__ void stage_x(const GemvParams& p, const Io& io, __half* xs, int k_lo,
         if (m < M) v[m] = __ldcg(reinterpret_cast<const uint4*>(io.x + (size_t)m * io.ldx + k_lo + c * 8));
 #pragma unroll
       for (int m = 0; m < 8; ++m)
-        if (m < M) sts128(xs + (size_t)m * p.x_rs + c * 8, v[m]);
+        if (m < M) {
+          sts128(xs + (size_t)m * p.x_rs + c * 8, v[m]);
+          if (red) {
+            const float2 a = h2_to_f2(v[m].x), b = h2_to_f2(v[m].y), cc = h2_to_f2(v[m].z), d = h2_to_f2(v[m].w);
+            float t = a.x * a.x;
+            t = fmaf(a.y, a.y, t); t = fmaf(b.x, b.x, t); t = fmaf(b.y, b.y, t);
+            t = fmaf(cc.x, cc.x, t); t = fmaf(cc.y, cc.y, t); t = fmaf(d.x, d.x, t); t = fmaf(d.y, d.y, t);
+            ss[m] += t;
+          }
+        }
     }
   } else {
     // Unaligned rows or a range past K: element loads, zero past K.
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      if (m < M) {
+        const __half* row = io.x + (size_t)m * io.ldx;
 #pragma unroll 1
-    for (int m = 0; m < M; ++m) {
-      const __half* row = io.x + (size_t)m * io.ldx;
-#pragma unroll 1
-      for (int k = k_lo + tid; k < k_lo + krange; k += NT)
-        xs[(size_t)m * p.x_rs + (k - k_lo)] = k < K ? __ldcg(row + k) : __float2half(0.f);
+        for (int k = k_lo + tid; k < k_lo + krange; k += NT) {
+          const __half v = k < K ? __ldcg(row + k) : __float2half(0.f);
+          xs[(size_t)m * p.x_rs + (k - k_lo)] = v;
+          const float f = __half2float(v);
+          ss[m] = fmaf(f, f, ss[m]);
+        }
+      }
     }
   }
-}
-
-// Partial sums of squares of the staged rows for RMSNorm (gamma = 1), all
-// warps at once: row m is split over W / M warps, warp part i of row m
-// writing red[m * W + i]; rms_of() adds the parts in order (deterministic).
-// Requires the full row in shared memory (k_lo == 0, zero padding past K).
-__device__ __forceinline__ void rms_partials(const GemvParams& p, const __half* xs, float* red, int warp,
-                                             int lane) {
-  const int parts = W / p.M;
-  const int m = warp / parts, part = warp - m * parts;
-  if (m >= p.M) return;
-  const __half* row = xs + (size_t)m * p.x_rs;
-  const int nch = p.K / 8;
-  float s0 = 0.f, s1 = 0.f;
-  for (int c = part * 32 + lane; c < nch; c += parts * 32) {
-    const uint4 v = lds128(row + c * 8);
-    const float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), cc = h2_to_f2(v.z), d = h2_to_f2(v.w);
-    s0 = fmaf(a.x, a.x, s0); s1 = fmaf(a.y, a.y, s1); s0 = fmaf(b.x, b.x, s0); s1 = fmaf(b.y, b.y, s1);
-    s0 = fmaf(cc.x, cc.x, s0); s1 = fmaf(cc.y, cc.y, s1); s0 = fmaf(d.x, d.x, s0); s1 = fmaf(d.y, d.y, s1);
-  }
-  float s = s0 + s1;
+  if (red) {
+    const int lane = tid & 31, warp = tid >> 5;
 #pragma unroll
-  for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if (lane == 0) red[m * W + part] = s;
+    for (int off = 16; off; off >>= 1)
+#pragma unroll
+      for (int m = 0; m < 8; ++m) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], off);
+    if (lane < 8) {
+      float t = ss[0];
+#pragma unroll
+      for (int m = 1; m < 8; ++m) t = lane == m ? ss[m] : t;
+      red[warp * 8 + lane] = t;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -465,6 +480,10 @@ struct Range {
 
 __device__ __forceinline__ Range cta_range(const GemvParams& p, int warp) {
   Range r;
+  if ((int)blockIdx.x >= p.grid) {  // a launch wider than this phase's plan
+    r.u0 = r.u1 = r.n_mine = 0;
+    return r;
+  }
   r.u0 = range_start(p, blockIdx.x);
   r.u1 = range_start(p, blockIdx.x + 1);
   const int n = r.u1 - r.u0;
@@ -496,7 +515,7 @@ __device__ __forceinline__ void prefetch_phase(const GemvParams& p, const uint8_
 // issues bulk prefetches; no registers, no completion to wait for).
 __device__ __forceinline__ void l2_prefetch_phase(const GemvParams& p, const uint8_t* packed, int unit_bytes,
                                                   long long bytes) {
-  if (threadIdx.x != 0) return;
+  if (threadIdx.x != 0 || (int)blockIdx.x >= p.grid) return;
   const long long a = range_start(p, blockIdx.x);
   const long long b = range_start(p, blockIdx.x + 1);
   bytes = min(bytes, (b - a) * unit_bytes);
@@ -519,7 +538,7 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
   constexpr int UNIT = P * kUnitPlaneBytes;
   constexpr size_t WSTEP = (size_t)W * UNIT;
   constexpr int KPB = (WB == 1) ? 32 : 16;  // k per k-block
-  float* red = reinterpret_cast<float*>(smem + kOffRed);  // RMSNorm partial sums [8][W]
+  float* red = reinterpret_cast<float*>(smem + kOffRed);  // RMSNorm sums of squares [W][8]
   const Epi epi = epi_of(p, smem, P);
   float4* slots = reinterpret_cast<float4*>(smem + kOffSlots);  // [n_slots][W][P][32]
   __half* xs = reinterpret_cast<__half*>(smem + p.off_x);
@@ -538,12 +557,11 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
   // ---- activations
   if (tid == 0) STRACE(trace_base);
   if (active) {
-    stage_x(p, io, xs, k_lo, krange, tid);
+    stage_x(p, io, xs, k_lo, krange, tid, p.rmsnorm ? red : nullptr);
     load_epi<P>(p, io, epi, vt_first, vt_last - vt_first + 1, tid);
   }
   for (int i = tid; i < p.n_slots * W * P * 32; i += NT) slots[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   __syncthreads();
-  if (p.rmsnorm && active) rms_partials(p, xs, red, warp, lane);
   if (threadIdx.x == 0) {
     TRACE(2);
     STRACE(trace_base + 1);
@@ -812,9 +830,9 @@ cudaError_t launch_gemv(const GemvParams& p, int planes, int wbytes, int math, s
   return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_stack(const StackParams& sp, int wbytes, size_t smem, cudaStream_t stream) {
+cudaError_t launch_stack(const StackParams& sp, int grid, int wbytes, size_t smem, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(sp.gu.grid);
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;

@@ -22,8 +22,8 @@ constexpr int kTileCh = 16;
 constexpr int kWarps = 16;  // one CTA of 16 warps per SM
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxSlots = 8;  // virtual tiles one CTA may touch
-// Shared memory: [64,68) barrier verdict, [128,640) RMSNorm partial sums
-// [8 rows][16 warps], then the per-warp partial slots
+// Shared memory: [64,68) barrier verdict, [128,640) RMSNorm sums of squares
+// [16 warps][8 rows], then the per-warp partial slots
 // [n_slots][warps][planes][32 lanes][16 B], then the per-slot epilogue inputs
 // (scales [n_slots][planes][16], residual rows [n_slots][8][16], fp32), then
 // the x rows.
@@ -125,7 +125,8 @@ struct StackParams {
   unsigned* barrier;  // zero at launch; the kernel leaves it zero
   int n_layers;
 };
-cudaError_t launch_stack(const StackParams& sp, int wbytes, size_t smem, cudaStream_t stream);
+// grid >= both phases' planned grids; CTAs past a phase's grid idle in it.
+cudaError_t launch_stack(const StackParams& sp, int grid, int wbytes, size_t smem, cudaStream_t stream);
 // Largest grid of stack_kernel<wbytes> that can be co-resident with `smem` bytes per CTA.
 cudaError_t stack_max_coresident(int wbytes, size_t smem, int num_sms, int* max_grid);
 // Raises the dynamic shared-memory limit of every kernel variant.

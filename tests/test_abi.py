@@ -86,3 +86,10 @@ def test_package_does_not_reference_the_oracle():
     for p in list(pkg.rglob("*.py")) + list(pkg.rglob("*.cu")) + list(pkg.rglob("*.cpp")) + \
             list(pkg.rglob("*.cuh")) + list(pkg.rglob("*.h")):
         assert "oracle" not in p.read_text().lower(), p
+
+
+def test_refused_option_keeps_plan(b2g):
+    """Options are validated without a GPU only as far as the arguments go;
+    an invalid key or value is refused before any CUDA call."""
+    L = b2g.lib()
+    assert L.b2g_op_set_option(None, b2g.OPT_GRID, 0) == b2g.ERR_INVALID

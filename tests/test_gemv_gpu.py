@@ -178,6 +178,47 @@ def test_partition_modes(b2g, orc, syn, cuda, part, K, N, fuse, grid):
     assert b2g.device_error() == 0
 
 
+@pytest.mark.parametrize("ks,part,grid", [(2, "units", 0), (2, "tiles", 0), (4, "units", 0), (4, "tiles", 0),
+                                           (8, "units", 296)])
+def test_ksplit_ranges(b2g, orc, syn, cuda, ks, part, grid):
+    """K cut into several ranges: every tile's ranges are summed across CTAs
+    (the residual op, so the finisher also adds the residual)."""
+    K, N = 8192, 3072
+    mode = {"units": b2g.PARTITION_UNITS, "tiles": b2g.PARTITION_TILES}[part]
+    Wd, Wh, s = make_weights(orc, syn, 37, K, N, 1, 3)
+    for M in (1, 8):
+        x = syn.activations(40 + M, M, K)
+        r = syn.activations(50 + M, M, N)
+        op = b2g.GemvOp(K, N, weight_dtype=1, scale_mode=3, max_m=8, fuse=b2g.FUSE_RESIDUAL_ADD)
+        op.set_option(b2g.OPT_GRID, grid)
+        op.set_option(b2g.OPT_PARTITION, mode)
+        op.set_option(b2g.OPT_KSPLIT, ks)
+        assert op.plan(M)["ksplit"] == ks
+        packed = op.prepack(Wd)
+        y = op.enqueue(dev(x), packed, dev(s), residual=dev(r))
+        torch.cuda.synchronize()
+        want = orc.residual_add(r, orc.to_f16(orc.gemv(Wh, orc.WTYPE_FP8, x, 3, s))).astype(np.float64)
+        check(orc, y, want, 1, (ks, part, M))
+    assert b2g.device_error() == 0
+
+
+def test_refused_option_keeps_plan(b2g, orc, syn, cuda):
+    """8 K ranges on 148 CTAs would need more than 8 tiles per CTA: refused,
+    and the op keeps its previous, working plan."""
+    K, N = 8192, 3072
+    op = b2g.GemvOp(K, N, weight_dtype=1, scale_mode=3, max_m=8)
+    before = op.plan(8)
+    with pytest.raises(b2g.B2GError) as e:
+        op.set_option(b2g.OPT_KSPLIT, 8)
+    assert e.value.status == b2g.ERR_UNSUPPORTED
+    assert op.plan(8) == before
+    Wd, Wh, s = make_weights(orc, syn, 38, K, N, 1, 3)
+    x = syn.activations(60, 8, K)
+    y = op.enqueue(dev(x), op.prepack(Wd), dev(s))
+    torch.cuda.synchronize()
+    check(orc, y, orc.gemv(Wh, orc.WTYPE_FP8, x, 3, s), 1)
+
+
 def test_deterministic_and_rows_independent(b2g, orc, syn, cuda):
     K, N = 3072, 8192
     Wd, Wh, s = make_weights(orc, syn, 35, K, N, 1, 3)
