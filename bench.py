@@ -296,12 +296,15 @@ def run_ours(args):
         # rank 0, NCCL all-reduce of the partials per layer).
         import importlib
         st = None
-        tps = importlib.import_module("b2g.tp").TPStack(HIDDEN, INTER, LAYERS, rank=rank, world=world, max_m=M)
+        tps = importlib.import_module("b2g.tp").TPStack(HIDDEN, INTER, LAYERS, rank=rank, world=world, max_m=M,
+                                                        fused=args.tp_mode == "fused")
         gu_op, dn_op = tps.gate_up, tps.down
     want_ref = tp == 1 and not args.no_ref_kernels and REF_GPU_LIB.exists()
     layers = make_layers(b2g, torch, device, tp, rank, (gu_op, dn_op), M, keep_raw=want_ref)
     for i, L in enumerate(layers):
         (st or tps).set_layer(i, L["pgu"], L["sgu"], L["pd"], L["sd"])
+    if tps is not None and tps.fused:
+        tps.setup_comm(device)
     torch.cuda.synchronize()
 
     stream = torch.cuda.current_stream()
@@ -454,7 +457,8 @@ def run_ours(args):
                              f"fused gate||up 3072->2x8192 + SiLU*up -> down 8192->3072 + residual; "
                              f"E4M3 weights, per-channel FP32 scales, fp16 activations, fp32 accumulate"),
                 "hidden": HIDDEN, "intermediate": INTER, "layers": LAYERS, "m": M,
-                "parallelism": f"tp{tp}", "weights_per_step_bytes": bytes_rank * tp,
+                "parallelism": f"tp{tp}" + (f" ({args.tp_mode} all-reduce)" if tp > 1 else ""),
+                "weights_per_step_bytes": bytes_rank * tp,
                 "l2": (f"inputs larger than L2: {bytes_rank * tp / 1e9:.2f} GB of weights streamed per step "
                        "(L2 126 MB), no flush"),
                 "timing": "CUDA graph replay of one step" if graph is not None else "direct launches",
@@ -467,7 +471,7 @@ def run_ours(args):
             "e2e": {"value": round(e2e_value, 4), "unit": "TB/s", "h2d_bytes_per_step": 2 * M * HIDDEN,
                     "d2h_bytes_per_step": 2 * M * HIDDEN, "ms_per_step": round(ms_e2e, 5),
                     "path": ("pinned host h -> b2g_stack_enqueue (C ABI) -> pinned host h" if st is not None
-                             else "pinned host h -> b2g_enqueue_ex per layer + NCCL all-reduce -> pinned host h")},
+                             else f"pinned host h -> TPStack ({args.tp_mode} all-reduce) -> pinned host h")},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
@@ -495,6 +499,9 @@ def run_ours(args):
     if graph is not None:
         graph.reset()
         graph = None
+    if tps is not None and tps.fused:
+        dist.barrier()  # no rank unmaps a peer buffer another rank may still write
+        tps.close_comm()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -547,6 +554,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ref-kernels", action="store_true", help="skip timing the reference's GPU kernels")
+    ap.add_argument("--tp-mode", choices=["fused", "nccl"], default="fused",
+                    help="N > 1: all-reduce fused into the GEMVs over peer memory, or NCCL")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decode-MLP layers (28 = Llama-3.2-3B; fewer only for small profiling captures)")
     args = ap.parse_args()

@@ -230,6 +230,61 @@ b2g_status b2g_device_error(int32_t* code, int32_t clear);
 b2g_status b2g_enqueue_static(const b2g_op* op, const b2g_enqueue_args* args, b2g_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Tensor-parallel exchange through peer memory (no reference counterpart:
+ * the reference runs on one GPU).  One process per GPU.  Each rank allocates
+ * a zero-filled communication buffer of b2g_tp_comm_bytes(), shares it with
+ * b2g_ipc_handle / b2g_ipc_open, and fills a b2g_tp_comm with every rank's
+ * mapped addresses (b2g_tp_comm_layout).  Then, per layer:
+ *   down op, mode PUSH: instead of writing y, the epilogue stores this rank's
+ *     output rows straight into its slot of every rank's inbox (NVLink peer
+ *     stores); each CTA then fences at system scope once and adds one
+ *     arrival on every rank's counter;
+ *   next gate||up op, mode GATHER: its activation staging waits (bounded)
+ *     for all ranks' arrivals, sums the slots in rank order (fp32, one fp16
+ *     rounding: every rank gets bitwise the same rows) and writes the sum to
+ *     h_out (the residual input of the next down op).
+ * After the last layer b2g_tp_gather writes the final rows.  Consecutive
+ * layers alternate between the inbox's two buffers (`buf`).  A wait that
+ * expires sets the device error word (B2G_ERR_PEER_TIMEOUT class, code 4).
+ * ------------------------------------------------------------------------ */
+#define B2G_TP_MAX_RANKS 8
+enum { B2G_TP_NONE = 0, B2G_TP_PUSH = 1, B2G_TP_GATHER = 2 };
+typedef struct {
+  int32_t world, rank;
+  int32_t max_m;   /* rows per inbox slot */
+  int32_t width;   /* halves per row (the hidden size, a multiple of 8) */
+  void* inbox[B2G_TP_MAX_RANKS];    /* every rank's inbox, mapped in this process */
+  void* counters[B2G_TP_MAX_RANKS]; /* every rank's arrival counters */
+  void* epoch;                      /* this rank's launch counter */
+} b2g_tp_comm;
+/* Bytes of one rank's communication buffer (inbox [2][world][max_m][width]
+ * fp16, counters [world] u32, epoch u32), and the addresses inside a buffer
+ * at `base` (the same layout on every rank). */
+size_t b2g_tp_comm_bytes(int32_t world, int32_t max_m, int32_t width);
+b2g_status b2g_tp_comm_layout(void* base, int32_t world, int32_t max_m, int32_t width, void** inbox,
+                              void** counters, void** epoch);
+/* CUDA IPC of a device buffer: a B2G_IPC_RECORD_BYTES record (the handle of
+ * the allocation holding dev_ptr and dev_ptr's offset in it, so buffers from
+ * a caching allocator work), opened in another process on its own device;
+ * b2g_ipc_close takes the address b2g_ipc_open returned. */
+#define B2G_IPC_RECORD_BYTES 72
+b2g_status b2g_ipc_handle(const void* dev_ptr, void* record);
+b2g_status b2g_ipc_open(const void* record, void** dev_ptr);
+b2g_status b2g_ipc_close(void* dev_ptr);
+/* b2g_enqueue_ex with an exchange mode.  PUSH: the op must not fuse gate||up;
+ * args->y is not written.  GATHER: the op's rows must be whole (K split 1),
+ * K == comm->width; args->x is not read; push_op is the op whose launches push
+ * (its CTA count is the arrival count per round); h_out [m, ldh] receives the
+ * summed rows. */
+b2g_status b2g_enqueue_tp(const b2g_op* op, const b2g_enqueue_args* args, const b2g_tp_comm* comm,
+                          int32_t mode, int32_t buf, const b2g_op* push_op, void* h_out, int64_t ldh,
+                          b2g_stream_t stream);
+/* h [m, ldh] = sum of the inbox slots of buffer `buf` once every rank's
+ * pushing launch of this round (push_op's) has arrived. */
+b2g_status b2g_tp_gather(const b2g_tp_comm* comm, int32_t buf, const b2g_op* push_op, int32_t m, void* h,
+                         int64_t ldh, b2g_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Decode MLP stack: n_layers x [RMSNorm -> fused gate||up + SiLU*up -> down +
  * residual], hidden state updated in place.  No reference counterpart (the
  * reference runs single GEMVs); the layer dataflow is its ONNX graph's

@@ -72,6 +72,16 @@ class StackFields(ctypes.Structure):
                 ("rms_eps", ctypes.c_float), ("tp_rank", ctypes.c_int32), ("tp_size", ctypes.c_int32)]
 
 
+TP_NONE, TP_PUSH, TP_GATHER = 0, 1, 2
+TP_MAX_RANKS = 8
+
+
+class TpComm(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("max_m", ctypes.c_int32),
+                ("width", ctypes.c_int32), ("inbox", ctypes.c_void_p * TP_MAX_RANKS),
+                ("counters", ctypes.c_void_p * TP_MAX_RANKS), ("epoch", ctypes.c_void_p)]
+
+
 # Every exported entry point and its ctypes signature (kept in step with
 # include/b200gemv.h; the tests check the two agree).
 _P, _I32, _I64, _SZ = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
@@ -91,6 +101,15 @@ SIGNATURES = {
     "b2g_enqueue_ex": ([_P, ctypes.POINTER(EnqueueArgs), _P], ctypes.c_int),
     "b2g_device_error": ([ctypes.POINTER(_I32), _I32], ctypes.c_int),
     "b2g_enqueue_static": ([_P, ctypes.POINTER(EnqueueArgs), _P], ctypes.c_int),
+    "b2g_tp_comm_bytes": ([_I32, _I32, _I32], _SZ),
+    "b2g_tp_comm_layout": ([_P, _I32, _I32, _I32, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P)],
+                           ctypes.c_int),
+    "b2g_ipc_handle": ([_P, _P], ctypes.c_int),
+    "b2g_ipc_open": ([_P, ctypes.POINTER(_P)], ctypes.c_int),
+    "b2g_ipc_close": ([_P], ctypes.c_int),
+    "b2g_enqueue_tp": ([_P, ctypes.POINTER(EnqueueArgs), ctypes.POINTER(TpComm), _I32, _I32, _P, _P, _I64, _P],
+                       ctypes.c_int),
+    "b2g_tp_gather": ([ctypes.POINTER(TpComm), _I32, _P, _I32, _P, _I64, _P], ctypes.c_int),
     "b2g_stack_create": ([ctypes.POINTER(StackFields), ctypes.POINTER(_P)], ctypes.c_int),
     "b2g_stack_destroy": ([_P], ctypes.c_int),
     "b2g_stack_ops": ([_P, ctypes.POINTER(_P), ctypes.POINTER(_P)], ctypes.c_int),
@@ -229,6 +248,26 @@ class GemvOp:
         check(lib().b2g_enqueue_ex(self.h, ctypes.byref(a), _stream(stream)), "b2g_enqueue_ex")
         return y
 
+    def enqueue_tp(self, comm, mode, buf, x, packed, scales=None, y=None, workspace=None, residual=None,
+                   rms_eps: float = 1e-5, pdl: bool = False, stream=None, prefetch=None, push_op=None,
+                   h_out=None):
+        """b2g_enqueue_tp: PUSH (this op's rows to every rank's inbox) or GATHER
+        (stage the all-reduced rows from the local inbox, writing them to h_out)."""
+        m = x.shape[0]
+        a = EnqueueArgs(m, x.data_ptr(), _rows_stride(x), packed.data_ptr(),
+                        0 if scales is None else scales.data_ptr(),
+                        0 if residual is None else residual.data_ptr(),
+                        0 if residual is None else _rows_stride(residual),
+                        (x if y is None else y).data_ptr(), self.N if y is None else _rows_stride(y),
+                        workspace.data_ptr(), rms_eps, 1 if pdl else 0,
+                        None if prefetch is None else prefetch[1].data_ptr(),
+                        None if prefetch is None else prefetch[0].h)
+        check(lib().b2g_enqueue_tp(self.h, ctypes.byref(a), ctypes.byref(comm), mode, buf,
+                                   None if push_op is None else push_op.h,
+                                   None if h_out is None else h_out.data_ptr(),
+                                   0 if h_out is None else _rows_stride(h_out), _stream(stream)),
+              "b2g_enqueue_tp")
+
     def enqueue_static(self, x, packed, y, scales=None, residual=None, rms_eps: float = 1e-5,
                        stream=None):
         """y = op(x, W, scales) on the library's static scratch (b2g_enqueue_static).
@@ -322,3 +361,41 @@ class Stack:
         check(lib().b2g_stack_enqueue(self.h, h.shape[0], _ptr(h), _ptr(act), _ptr(workspace),
                                       _stream(stream)), "b2g_stack_enqueue")
         return h
+
+
+def tp_comm_bytes(world: int, max_m: int, width: int) -> int:
+    return lib().b2g_tp_comm_bytes(world, max_m, width)
+
+
+def tp_comm_layout(base: int, world: int, max_m: int, width: int):
+    """(inbox, counters, epoch) device addresses inside a comm buffer at base."""
+    i, c, e = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+    check(lib().b2g_tp_comm_layout(ctypes.c_void_p(base), world, max_m, width, ctypes.byref(i),
+                                   ctypes.byref(c), ctypes.byref(e)), "b2g_tp_comm_layout")
+    return i.value, c.value, e.value
+
+
+IPC_RECORD_BYTES = 72
+
+
+def ipc_handle(t) -> bytes:
+    buf = ctypes.create_string_buffer(IPC_RECORD_BYTES)
+    check(lib().b2g_ipc_handle(ctypes.c_void_p(t.data_ptr()), buf), "b2g_ipc_handle")
+    return buf.raw
+
+
+def ipc_open(record: bytes) -> int:
+    p = ctypes.c_void_p()
+    check(lib().b2g_ipc_open(ctypes.create_string_buffer(record, IPC_RECORD_BYTES), ctypes.byref(p)),
+          "b2g_ipc_open")
+    return p.value
+
+
+def ipc_close(addr: int):
+    check(lib().b2g_ipc_close(ctypes.c_void_p(addr)), "b2g_ipc_close")
+
+
+def tp_gather(comm, buf: int, push_op, h, stream=None):
+    check(lib().b2g_tp_gather(ctypes.byref(comm), buf, push_op.h, h.shape[0], ctypes.c_void_p(h.data_ptr()),
+                              _rows_stride(h), _stream(stream)), "b2g_tp_gather")
+    return h

@@ -400,7 +400,15 @@ b2g_status b2g_workspace_init(const b2g_op* op, void* ws, b2g_stream_t stream) {
   return cuda_status(cudaMemsetAsync(ws, 0, bytes, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+static b2g_status enqueue_impl(const b2g_op* op, const b2g_enqueue_args* a, const TpParams* tp,
+                               b2g_stream_t stream);
+
 b2g_status b2g_enqueue_ex(const b2g_op* op, const b2g_enqueue_args* a, b2g_stream_t stream) {
+  return enqueue_impl(op, a, nullptr, stream);
+}
+
+static b2g_status enqueue_impl(const b2g_op* op, const b2g_enqueue_args* a, const TpParams* tp,
+                               b2g_stream_t stream) {
   if (!op || !a) return B2G_ERR_INVALID;
   if (a->m < 1 || a->m > op->f.max_m) return B2G_ERR_INVALID;
   if (!a->x || !a->packed_w || !a->y || !a->workspace) return B2G_ERR_INVALID;
@@ -440,6 +448,7 @@ b2g_status b2g_enqueue_ex(const b2g_op* op, const b2g_enqueue_args* a, b2g_strea
     p.pf_grid = nx->grid;
     p.pf_bytes = 1 << 30;  // the CTA's whole range
   }
+  if (tp) p.tp = *tp;
   return cuda_status(launch_gemv(p, op->planes, op->wbytes, op->math, lp.smem, a->pdl != 0,
                                  reinterpret_cast<cudaStream_t>(stream)));
 }
@@ -515,6 +524,153 @@ b2g_status b2g_enqueue_static(const b2g_op* op, const b2g_enqueue_args* args, b2
   a.workspace = ws;
   a.pdl = 0;
   return b2g_enqueue_ex(op, &a, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-parallel exchange through peer memory
+// ---------------------------------------------------------------------------
+static size_t tp_inbox_bytes(int world, int max_m, int width) {
+  return ((size_t)2 * world * max_m * width * 2 + 255) / 256 * 256;
+}
+
+size_t b2g_tp_comm_bytes(int32_t world, int32_t max_m, int32_t width) {
+  if (world < 1 || world > B2G_TP_MAX_RANKS || max_m < 1 || width < 8) return 0;
+  return tp_inbox_bytes(world, max_m, width) + 256 + 256;
+}
+
+b2g_status b2g_tp_comm_layout(void* base, int32_t world, int32_t max_m, int32_t width, void** inbox,
+                              void** counters, void** epoch) {
+  if (!base || !inbox || !counters || !epoch || b2g_tp_comm_bytes(world, max_m, width) == 0) return B2G_ERR_INVALID;
+  uint8_t* b = static_cast<uint8_t*>(base);
+  const size_t ib = tp_inbox_bytes(world, max_m, width);
+  *inbox = b;
+  *counters = b + ib;
+  *epoch = b + ib + 256;
+  return B2G_OK;
+}
+
+// An IPC handle names a whole allocation; a caching allocator may hand out
+// a buffer inside a larger one, so the record also carries the offset from
+// the allocation's base (cuMemGetAddressRange, through the driver entry point).
+using MemGetAddressRangeFn = int (*)(unsigned long long* base, size_t* size, unsigned long long ptr);
+
+static MemGetAddressRangeFn get_address_range_fn() {
+  static MemGetAddressRangeFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<MemGetAddressRangeFn>(p);
+  }();
+  return fn;
+}
+
+static std::mutex g_ipc_mu;
+static std::vector<std::pair<void*, void*>> g_ipc_open;  // (returned address, mapped base)
+
+b2g_status b2g_ipc_handle(const void* dev_ptr, void* record) {
+  if (!dev_ptr || !record) return B2G_ERR_INVALID;
+  static_assert(sizeof(cudaIpcMemHandle_t) + 8 == B2G_IPC_RECORD_BYTES, "IPC record size");
+  const MemGetAddressRangeFn range = get_address_range_fn();
+  if (!range) return B2G_ERR_CUDA;
+  unsigned long long base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<unsigned long long>(dev_ptr)) != 0) return B2G_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return B2G_ERR_CUDA;
+  const uint64_t off = reinterpret_cast<unsigned long long>(dev_ptr) - base;
+  std::memcpy(record, &h, sizeof(h));
+  std::memcpy(static_cast<uint8_t*>(record) + sizeof(h), &off, 8);
+  return B2G_OK;
+}
+
+b2g_status b2g_ipc_open(const void* record, void** dev_ptr) {
+  if (!record || !dev_ptr) return B2G_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  uint64_t off = 0;
+  std::memcpy(&h, record, sizeof(h));
+  std::memcpy(&off, static_cast<const uint8_t*>(record) + sizeof(h), 8);
+  void* base = nullptr;
+  if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return B2G_ERR_CUDA;
+  *dev_ptr = static_cast<uint8_t*>(base) + off;
+  std::lock_guard<std::mutex> lk(g_ipc_mu);
+  g_ipc_open.emplace_back(*dev_ptr, base);
+  return B2G_OK;
+}
+
+b2g_status b2g_ipc_close(void* dev_ptr) {
+  if (!dev_ptr) return B2G_ERR_INVALID;
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_ipc_mu);
+    for (size_t i = 0; i < g_ipc_open.size(); ++i)
+      if (g_ipc_open[i].first == dev_ptr) {
+        base = g_ipc_open[i].second;
+        g_ipc_open.erase(g_ipc_open.begin() + i);
+        break;
+      }
+  }
+  if (!base) return B2G_ERR_INVALID;
+  return cuda_status(cudaIpcCloseMemHandle(base));
+}
+
+static b2g_status fill_tp(const b2g_tp_comm* c, int mode, int buf, const b2g_op* push_op, void* h_out,
+                          int64_t ldh, int m, TpParams* tp) {
+  if (!c || !push_op || c->world < 1 || c->world > B2G_TP_MAX_RANKS || c->rank < 0 || c->rank >= c->world)
+    return B2G_ERR_INVALID;
+  if ((buf != 0 && buf != 1) || c->width % 8 != 0 || m > c->max_m || !c->epoch) return B2G_ERR_INVALID;
+  for (int r = 0; r < c->world; ++r)
+    if (!c->inbox[r] || !c->counters[r] || !aligned(c->inbox[r], 16) || !aligned(c->counters[r], 4))
+      return B2G_ERR_INVALID;
+  if (mode == B2G_TP_GATHER && (!h_out || !aligned(h_out, 16) || ldh < c->width || ldh % 8 != 0))
+    return B2G_ERR_INVALID;
+  *tp = TpParams{};
+  tp->mode = mode;
+  tp->world = c->world;
+  tp->rank = c->rank;
+  tp->buf = buf;
+  tp->push_grid = push_op->grid;
+  tp->inbox_m = c->max_m;
+  tp->width = c->width;
+  for (int r = 0; r < c->world; ++r) {
+    tp->inbox[r] = static_cast<__half*>(c->inbox[r]);
+    tp->counters[r] = static_cast<unsigned*>(c->counters[r]);
+  }
+  tp->epoch = static_cast<unsigned*>(c->epoch);
+  tp->h_out = static_cast<__half*>(h_out);
+  tp->ldh = ldh;
+  return B2G_OK;
+}
+
+b2g_status b2g_enqueue_tp(const b2g_op* op, const b2g_enqueue_args* a, const b2g_tp_comm* comm, int32_t mode,
+                          int32_t buf, const b2g_op* push_op, void* h_out, int64_t ldh, b2g_stream_t stream) {
+  if (!op || !a || !comm) return B2G_ERR_INVALID;
+  if (mode == B2G_TP_PUSH) {
+    if (op->planes != 1 || op->N != comm->width || op->N % kTileCh != 0) return B2G_ERR_INVALID;
+    push_op = op;
+  } else if (mode == B2G_TP_GATHER) {
+    if (!push_op || op->ksplit != 1 || op->K != comm->width || op->K % 32 != 0) return B2G_ERR_INVALID;
+  } else {
+    return B2G_ERR_INVALID;
+  }
+  TpParams tp;
+  b2g_status st = fill_tp(comm, mode, buf, push_op, h_out, ldh, a->m, &tp);
+  if (st != B2G_OK) return st;
+  return enqueue_impl(op, a, &tp, stream);
+}
+
+b2g_status b2g_tp_gather(const b2g_tp_comm* comm, int32_t buf, const b2g_op* push_op, int32_t m, void* h,
+                         int64_t ldh, b2g_stream_t stream) {
+  if (!comm || !push_op || m < 1) return B2G_ERR_INVALID;
+  TpParams tp;
+  b2g_status st = fill_tp(comm, B2G_TP_GATHER, buf, push_op, h, ldh, m, &tp);
+  if (st != B2G_OK) return st;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B2G_ERR_CUDA;
+  st = ensure_device_setup(dev, push_op->smem_optin);
+  if (st != B2G_OK) return st;
+  return cuda_status(launch_tp_gather(tp, m, g_err_word[dev], reinterpret_cast<cudaStream_t>(stream)));
 }
 
 // ---------------------------------------------------------------------------

@@ -177,6 +177,21 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
   return old;
 }
 
+// Arrival on another GPU's counter, relaxed: the caller orders its earlier
+// stores with one fence.acq_rel.sys before its arrivals (a release form of
+// each arrival would repeat that system-scope fence per peer).
+__device__ __forceinline__ void red_relaxed_sys_add(unsigned* p, unsigned v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 // float -> E4M3 code, round to nearest even, saturate to +-448.
 __device__ __forceinline__ uint8_t f32_to_e4m3(float f) {
   uint16_t r;

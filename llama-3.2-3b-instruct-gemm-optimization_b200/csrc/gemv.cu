@@ -172,9 +172,10 @@ __device__ __forceinline__ float rms_of(const GemvParams& p, const float* red, i
 
 // red: RMSNorm partial sums (nullptr when the op has no RMSNorm); the
 // normalisation is linear, so it scales the accumulator: y = fp16(acc * r_m * s_n).
+// stage: 256 B of this warp's own shared memory, for PUSH rows.
 template <int P>
 __device__ __forceinline__ void epilogue(const GemvParams& p, const Io& io, int j, int tile, const float (&v)[P][4],
-                                         int lane, const float* red, const Epi& e) {
+                                         int lane, const float* red, const Epi& e, __half* stage) {
   const int g = lane >> 2, q = lane & 3;
   // this lane's two token rows, 2q and 2q + 1
   const float r0 = (red && 2 * q < p.M) ? rms_of(p, red, 2 * q) : 1.0f;
@@ -195,7 +196,22 @@ __device__ __forceinline__ void epilogue(const GemvParams& p, const Io& io, int 
         const float uf = __half2float(__float2half_rn(v[1][i] * r * e.scale[(j * 2 + 1) * 16 + c]));
         out = __float2half_rn(gf / (1.0f + __expf(-gf)) * uf);
       }
-      io.y[(size_t)m * io.ldy + n] = out;
+      if (P == 1 && p.tp.mode == kTpPush)
+        stage[m * 16 + c] = out;
+      else
+        io.y[(size_t)m * io.ldy + n] = out;
+    }
+  }
+  if (P == 1 && p.tp.mode == kTpPush) {
+    // The tile's rows are 32 B each: two lanes per row store 16 B into this
+    // rank's slot of every rank's inbox (peer stores over NVLink).
+    __syncwarp();
+    if (lane < 2 * p.M) {
+      const int m = lane >> 1, h = lane & 1;
+      const uint4 v16 = lds128(stage + m * 16 + h * 8);
+      const size_t off =
+          (((size_t)p.tp.buf * p.tp.world + p.tp.rank) * p.tp.inbox_m + m) * p.tp.width + tile * kTileCh + h * 8;
+      for (int r = 0; r < p.tp.world; ++r) *reinterpret_cast<uint4*>(p.tp.inbox[r] + off) = v16;
     }
   }
 }
@@ -205,7 +221,7 @@ __device__ __forceinline__ void epilogue(const GemvParams& p, const Io& io, int 
 // contributing CTA sum all partials in (k-range, CTA) order.
 template <int P>
 __device__ __forceinline__ void finish_vt(const GemvParams& p, const Io& io, int vt, int j, const float (&v)[P][4],
-                                          int lane, const float* red, const Epi& e) {
+                                          int lane, const float* red, const Epi& e, __half* stage) {
   const int ks = fdiv(vt, p.div_tiles);
   const int tile = vt - ks * p.n_tiles;
   // Contributors of k-range k: CTAs cta_of(a_k) .. cta_of(a_k + kbpv - 1).
@@ -269,7 +285,32 @@ __device__ __forceinline__ void finish_vt(const GemvParams& p, const Io& io, int
     }
     if (lane == 0) p.counters[tile] = 0;
   }
-  epilogue<P>(p, io, j, tile, s, lane, red, e);
+  epilogue<P>(p, io, j, tile, s, lane, red, e, stage);
+}
+
+// Sum of squares of 8 halves, in one fixed order (stage_x and gather_x share
+// it, so the plain and the all-reduced staging give bitwise the same norm).
+__device__ __forceinline__ float sumsq8(const uint4& v) {
+  const float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), c = h2_to_f2(v.z), d = h2_to_f2(v.w);
+  float t = a.x * a.x;
+  t = fmaf(a.y, a.y, t); t = fmaf(b.x, b.x, t); t = fmaf(b.y, b.y, t);
+  t = fmaf(c.x, c.x, t); t = fmaf(c.y, c.y, t); t = fmaf(d.x, d.x, t); t = fmaf(d.y, d.y, t);
+  return t;
+}
+
+// Per-thread row sums -> red[warp][m] (shuffle tree over the warp).
+__device__ __forceinline__ void reduce_rows(float (&ss)[8], int tid, float* red) {
+  const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+  for (int off = 16; off; off >>= 1)
+#pragma unroll
+    for (int m = 0; m < 8; ++m) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], off);
+  if (lane < 8) {
+    float t = ss[0];
+#pragma unroll
+    for (int m = 1; m < 8; ++m) t = lane == m ? ss[m] : t;
+    red[warp * 8 + lane] = t;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -302,13 +343,7 @@ __device__ void stage_x(const GemvParams& p, const Io& io, __half* xs, int k_lo,
       for (int m = 0; m < 8; ++m)
         if (m < M) {
           sts128(xs + (size_t)m * p.x_rs + c * 8, v[m]);
-          if (red) {
-            const float2 a = h2_to_f2(v[m].x), b = h2_to_f2(v[m].y), cc = h2_to_f2(v[m].z), d = h2_to_f2(v[m].w);
-            float t = a.x * a.x;
-            t = fmaf(a.y, a.y, t); t = fmaf(b.x, b.x, t); t = fmaf(b.y, b.y, t);
-            t = fmaf(cc.x, cc.x, t); t = fmaf(cc.y, cc.y, t); t = fmaf(d.x, d.x, t); t = fmaf(d.y, d.y, t);
-            ss[m] += t;
-          }
+          if (red) ss[m] += sumsq8(v[m]);
         }
     }
   } else {
@@ -327,19 +362,116 @@ __device__ void stage_x(const GemvParams& p, const Io& io, __half* xs, int k_lo,
       }
     }
   }
-  if (red) {
-    const int lane = tid & 31, warp = tid >> 5;
-#pragma unroll
-    for (int off = 16; off; off >>= 1)
-#pragma unroll
-      for (int m = 0; m < 8; ++m) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], off);
-    if (lane < 8) {
-      float t = ss[0];
-#pragma unroll
-      for (int m = 1; m < 8; ++m) t = lane == m ? ss[m] : t;
-      red[warp * 8 + lane] = t;
+  if (red) reduce_rows(ss, tid, red);
+}
+
+// Bounded wait (thread 0) until this rank's arrival counters all reach
+// epoch * push_grid: every rank's pushing launch of this round has finished
+// its stores.  Counters only grow; the comparison tolerates wrap-around.
+__device__ __forceinline__ bool tp_wait_arrivals(const TpParams& tp, int* err) {
+  const unsigned target = *reinterpret_cast<volatile unsigned*>(tp.epoch) * (unsigned)tp.push_grid;
+  const unsigned* cnt = tp.counters[tp.rank];
+  const unsigned long long t0 = globaltimer_ns();
+  for (int r = 0; r < tp.world; ++r) {
+    while ((int)(ld_acquire_sys(cnt + r) - target) < 0) {
+      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+        atomicCAS(err, 0, kErrPeerWait);
+        return false;
+      }
+      __nanosleep(64);
     }
   }
+  return true;
+}
+
+// Slot r of buffer buf at row m, halves [k0, k0 + 8).
+__device__ __forceinline__ const uint4* tp_slot(const TpParams& tp, int r, int m, int k0) {
+  const size_t slot = (size_t)tp.inbox_m * tp.width;
+  return reinterpret_cast<const uint4*>(tp.inbox[tp.rank] + ((size_t)tp.buf * tp.world + r) * slot +
+                                        (size_t)m * tp.width + k0);
+}
+
+__device__ __forceinline__ void add8(float (&a)[8], const uint4& v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = h2_to_f2(w[j]);
+    a[2 * j] += f.x;
+    a[2 * j + 1] += f.y;
+  }
+}
+
+__device__ __forceinline__ uint4 round8(const float (&a)[8]) {
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    __half2 h = __floats2half2_rn(a[2 * j], a[2 * j + 1]);
+    o[j] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Sum of inbox slots 0..world-1 at row m, halves [k0, k0 + 8), in rank order
+// in fp32, rounded once to fp16.
+__device__ __forceinline__ uint4 tp_sum8(const TpParams& tp, int m, int k0) {
+  float a[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) a[j] = 0.f;
+  for (int r = 0; r < tp.world; ++r) add8(a, __ldcg(tp_slot(tp, r, m, k0)));
+  return round8(a);
+}
+
+// GATHER staging: x = the all-reduced rows, written to tp.h_out as well (each
+// CTA writes the chunks c with c % grid == its index).  Same thread -> chunk
+// assignment, layout and sums of squares as stage_x (so the norm is bitwise
+// the plain path's); rows are whole (k_lo = 0, host-checked).  Rows go in
+// batches of 4, every rank's slot load of a batch issued before its sums.
+__device__ void gather_x(const GemvParams& p, __half* xs, int krange, int tid, float* red, volatile int* verdict) {
+  const int M = p.M;
+  if (tid == 0) *verdict = tp_wait_arrivals(p.tp, p.error) ? 1 : 0;
+  __syncthreads();
+  const int nch = krange / 8;
+  constexpr int B = 4;
+  float ss[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) ss[m] = 0.f;
+#pragma unroll 1
+  for (int c = tid; c < nch; c += NT) {
+#pragma unroll
+    for (int m0 = 0; m0 < 8; m0 += B) {
+      if (m0 < M) {
+        float a[B][8];
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) a[b][j] = 0.f;
+#pragma unroll
+        for (int r = 0; r < kMaxTp; ++r) {
+          if (r < p.tp.world) {
+            uint4 v[B];
+#pragma unroll
+            for (int b = 0; b < B; ++b)
+              if (m0 + b < M) v[b] = __ldcg(tp_slot(p.tp, r, m0 + b, c * 8));
+#pragma unroll
+            for (int b = 0; b < B; ++b)
+              if (m0 + b < M) add8(a[b], v[b]);
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          const int m = m0 + b;
+          if (m < M) {
+            const uint4 v = round8(a[b]);
+            sts128(xs + (size_t)m * p.x_rs + c * 8, v);
+            if (c % p.grid == (int)blockIdx.x)
+              *reinterpret_cast<uint4*>(p.tp.h_out + (size_t)m * p.tp.ldh + c * 8) = v;
+            if (red) ss[m] += sumsq8(v);
+          }
+        }
+      }
+    }
+  }
+  if (red) reduce_rows(ss, tid, red);
 }
 
 // ---------------------------------------------------------------------------
@@ -530,7 +662,12 @@ __device__ __forceinline__ void l2_prefetch_phase(const GemvParams& p, const uin
 // then: e.g. prefetch the next phase), then combine and finish the tiles.
 // Entry requires every thread of the CTA to be past its last read of the
 // shared slots and x rows of any earlier phase.
-template <int P, int WB, int MATH, int R, class AfterStream>
+struct NoHook {
+  template <class T>
+  __device__ __forceinline__ void operator()(T&) const {}
+};
+
+template <int P, int WB, int MATH, int R, class AfterStream, bool TP>
 __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uint8_t* smem,
                                           uint4 (&ring)[R], uint64_t pol, AfterStream after_stream,
                                           int trace_base = -1) {
@@ -556,8 +693,14 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
 
   // ---- activations
   if (tid == 0) STRACE(trace_base);
+  const bool gather = TP && p.tp.mode == kTpGather;
+  if (gather) {
+    // every CTA takes part (the wait and the write-back of the reduced rows)
+    gather_x(p, xs, active ? krange : p.K / 8 * 8, tid, p.rmsnorm ? red : nullptr,
+             reinterpret_cast<volatile int*>(smem + kOffMisc));
+  }
   if (active) {
-    stage_x(p, io, xs, k_lo, krange, tid, p.rmsnorm ? red : nullptr);
+    if (!gather) stage_x(p, io, xs, k_lo, krange, tid, p.rmsnorm ? red : nullptr);
     load_epi<P>(p, io, epi, vt_first, vt_last - vt_first + 1, tid);
   }
   for (int i = tid; i < p.n_slots * W * P * 32; i += NT) slots[i] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -667,7 +810,10 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
         v[pl][3] += t.w;
       }
     }
-    finish_vt<P>(p, io, vt_first + j, j, v, lane, p.rmsnorm ? red : nullptr, epi);
+    // slot j's shared memory is this warp's alone once summed: the PUSH stage
+    __syncwarp();
+    finish_vt<P>(p, io, vt_first + j, j, v, lane, p.rmsnorm ? red : nullptr, epi,
+                 reinterpret_cast<__half*>(slots + (size_t)j * W * P * 32));
   }
 #ifdef B2G_TRACE
   __syncthreads();
@@ -705,7 +851,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_
   pdl_launch_dependents();
   pdl_wait();
   if (tid == 0) TRACE(1);
-  run_phase<P, WB, MATH, R>(p, io_of_params(p), smem, ring, pol, [](uint4 (&)[R]) {});
+  if (p.tp.mode == kTpPush && blockIdx.x == 0 && tid == 0) atomicAdd(p.tp.epoch, 1u);
+  run_phase<P, WB, MATH, R, NoHook, true>(p, io_of_params(p), smem, ring, pol, NoHook{});
+  if (p.tp.mode == kTpPush) {
+    // This CTA's peer stores are done: one arrival on every rank.
+    __syncthreads();
+    if (tid == 0) {
+      fence_acq_rel_sys();  // the CTA's peer stores (ordered by the barrier) before the arrivals
+      for (int r = 0; r < p.tp.world; ++r) red_relaxed_sys_add(p.tp.counters[r] + p.tp.rank, 1u);
+    }
+  }
   if (tid == 0) TRACE(4);
 }
 
@@ -779,7 +934,7 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
     // weights go to L2 meanwhile.
     l2_prefetch_phase(dn, L.pd, kUnitPlaneBytes, kWholeRange);
     const Io io_gu{L.pgu, L.sgu, sp.h, sp.ldh, nullptr, 0, sp.act, sp.ldact};
-    run_phase<2, WB, kMathMma, R>(gu, io_gu, smem, ring, pol, [](uint4 (&)[R]) {}, 8 * l);
+    run_phase<2, WB, kMathMma, R, NoHook, false>(gu, io_gu, smem, ring, pol, NoHook{}, 8 * l);
     // The ring is free again: the down phase's first units load while the
     // barrier completes.
     prefetch_phase<1, R>(dn, L.pd, ring, warp, lane, pol);
@@ -787,7 +942,7 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
     // h = h + act . Wd; the next layer's gate||up weights go to L2 meanwhile.
     if (more) l2_prefetch_phase(gu, next_gu, 2 * kUnitPlaneBytes, kWholeRange);
     const Io io_dn{L.pd, L.sd, sp.act, sp.ldact, sp.h, sp.ldh, sp.h, sp.ldh};
-    run_phase<1, WB, kMathMma, R>(dn, io_dn, smem, ring, pol, [](uint4 (&)[R]) {}, 8 * l + 4);
+    run_phase<1, WB, kMathMma, R, NoHook, false>(dn, io_dn, smem, ring, pol, NoHook{}, 8 * l + 4);
     if (more) {
       prefetch_phase<2, R>(gu, next_gu, ring, warp, lane, pol);
       if (!grid_barrier(sp.barrier, (++nbar) * G, gu.error, verdict)) return;
@@ -853,6 +1008,27 @@ cudaError_t stack_max_coresident(int wbytes, size_t smem, int num_sms, int* max_
                   : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stack_kernel<2>, kThreads, smem);
   *max_grid = per_sm * num_sms;
   return e;
+}
+
+namespace {
+__global__ void __launch_bounds__(256) tp_gather_kernel(const __grid_constant__ TpParams tp, int m_rows, int* err) {
+  __shared__ int verdict;
+  if (threadIdx.x == 0) verdict = tp_wait_arrivals(tp, err) ? 1 : 0;
+  __syncthreads();
+  if (!verdict) return;  // reported through the error word; h is left as it was
+  const int nch = tp.width / 8;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < m_rows * nch; i += gridDim.x * blockDim.x) {
+    const int m = i / nch, c = i - m * nch;
+    *reinterpret_cast<uint4*>(tp.h_out + (size_t)m * tp.ldh + c * 8) = tp_sum8(tp, m, c * 8);
+  }
+}
+}  // namespace
+
+cudaError_t launch_tp_gather(const TpParams& tp, int m, int* error, cudaStream_t stream) {
+  const int chunks = m * (tp.width / 8);
+  const int blocks = min(148, (chunks + 255) / 256);
+  tp_gather_kernel<<<blocks, 256, 0, stream>>>(tp, m, error);
+  return cudaGetLastError();
 }
 
 #ifdef B2G_TRACE

@@ -39,6 +39,31 @@ constexpr int kMaxTiles = kBarrierWordOffset / 4;
 
 enum MathKind : int { kMathMma = 0, kMathFfma = 1 };
 
+// Tensor-parallel exchange through peer memory (one process per GPU).  Each
+// rank owns an inbox [2 buffers][world][max_m][width] fp16 and arrival
+// counters [world]; peers' inboxes and counters are mapped into this
+// process.  PUSH: the epilogue stores this rank's output rows into slot
+// `rank` of buffer `buf` of every rank's inbox, then every CTA releases one
+// arrival on every rank's counter[rank] at system scope.  GATHER: the
+// activation staging waits (bounded) until every counter reaches
+// epoch * push_grid, then sums slots 0..world-1 of buffer `buf` in rank order
+// (fp32, one fp16 rounding) and writes the sum to h_out as it stages it.
+constexpr int kMaxTp = 8;
+enum TpMode : int { kTpNone = 0, kTpPush = 1, kTpGather = 2 };
+struct TpParams {
+  int mode;
+  int world, rank;
+  int buf;
+  int push_grid;      // CTAs of each rank's pushing launch (one plan on every rank)
+  int inbox_m;        // max_m rows per slot
+  int width;          // halves per row (the hidden size)
+  __half* inbox[kMaxTp];     // every rank's inbox (this rank's entry is local)
+  unsigned* counters[kMaxTp];  // every rank's arrival counters [world]
+  unsigned* epoch;           // this rank's count of pushing launches
+  __half* h_out;             // GATHER: the reduced rows [m, ldh] (this rank's memory)
+  long long ldh;
+};
+
 // Division of x < 2^31 by a divisor fixed per launch, as a multiply-high and
 // a shift (Granlund & Montgomery, "Division by invariant integers using
 // multiplication", 1994, fig. 4.1 with N = 32):
@@ -97,7 +122,12 @@ struct GemvParams {
   int pf_unit_bytes;
   int pf_grid;
   int pf_bytes;
+  TpParams tp;
 };
+
+// Final gather of a tensor-parallel chain: h = sum of the inbox slots once
+// every rank's last push has arrived (TpParams as for GATHER).
+cudaError_t launch_tp_gather(const TpParams& tp, int m, int* error, cudaStream_t stream);
 
 // Launch one GEMV (planes = 1 or 2, wbytes = 1 for E4M3 or 2 for FP16).
 cudaError_t launch_gemv(const GemvParams& p, int planes, int wbytes, int math, size_t smem,

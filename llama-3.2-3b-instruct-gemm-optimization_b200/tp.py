@@ -13,12 +13,16 @@ the reference runs on one GPU):
   h + down(act) with the residual counted once.
 
 RMSNorm runs replicated (each rank normalises the same h).  The GEMVs run in
-the C-ABI library (``GemvOp``); torch.distributed (NCCL on GPUs) carries the
-all-reduce.
+the C-ABI library (``GemvOp``).  The all-reduce is either
+torch.distributed's (NCCL on GPUs), or -- ``fused=True`` -- fused into the
+GEMVs through peer memory: the down GEMV's epilogue stores its rows into
+every rank's inbox over NVLink, and the next layer's gate||up GEMV sums the
+inbox slots in rank order while it stages its activations (b2g_enqueue_tp).
 """
 from __future__ import annotations
 
-from . import FUSE_GATE_UP_SILU, FUSE_NONE, FUSE_RESIDUAL_ADD, FUSE_RMSNORM_INPUT, GemvOp
+from . import (FUSE_GATE_UP_SILU, FUSE_NONE, FUSE_RESIDUAL_ADD, FUSE_RMSNORM_INPUT, TP_GATHER, TP_PUSH,
+               GemvOp, TpComm, ipc_close, ipc_handle, ipc_open, tp_comm_bytes, tp_comm_layout, tp_gather)
 
 
 def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
@@ -37,7 +41,8 @@ class TPStack:
 
     def __init__(self, hidden: int = 3072, intermediate: int = 8192, n_layers: int = 28,
                  rank: int = 0, world: int = 1, weight_dtype="fp8_e4m3", scale_mode="channel_fp32",
-                 max_m: int = 8, rms_eps: float = 1e-5, group=None, build_ops: bool = True):
+                 max_m: int = 8, rms_eps: float = 1e-5, group=None, build_ops: bool = True,
+                 fused: bool = False):
         self.hidden, self.intermediate, self.n_layers = hidden, intermediate, n_layers
         self.rank, self.world, self.group = rank, world, group
         self.lo, self.hi = shard_range(intermediate, rank, world)
@@ -45,6 +50,10 @@ class TPStack:
         self.max_m, self.rms_eps = max_m, rms_eps
         self.layers = [None] * n_layers
         self.gate_up = self.down = None
+        self.fused = fused
+        self.comm = None
+        self._comm_buf = None
+        self._peer_bases = []
         if build_ops:
             kw = dict(weight_dtype=weight_dtype, scale_mode=scale_mode, max_m=max_m,
                       tp_rank=rank, tp_size=world)
@@ -112,6 +121,66 @@ class TPStack:
 
     def enqueue(self, h, act, workspace):
         """All layers on h [M, hidden] fp16 in place; act is [M, I/tp] scratch."""
+        if self.fused:
+            return self._enqueue_fused(h, act, workspace)
         for layer in range(self.n_layers):
             self.layer_step(layer, h, act, workspace)
+        return h
+
+    # -- the all-reduce fused into the GEMVs -------------------------------------
+    def setup_comm(self, device="cuda"):
+        """Allocate this rank's zero-filled exchange buffer, share it with the
+        other ranks (CUDA IPC) and map theirs.  Collective: every rank calls it."""
+        import torch
+        import torch.distributed as dist
+        nbytes = tp_comm_bytes(self.world, self.max_m, self.hidden)
+        self._comm_buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        torch.cuda.synchronize()
+        handles = [ipc_handle(self._comm_buf)]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, ipc_handle(self._comm_buf), group=self.group)
+        comm = TpComm()
+        comm.world, comm.rank, comm.max_m, comm.width = self.world, self.rank, self.max_m, self.hidden
+        for r in range(self.world):
+            if r == self.rank:
+                base = self._comm_buf.data_ptr()
+            else:
+                base = ipc_open(handles[r])
+                self._peer_bases.append(base)
+            inbox, counters, epoch = tp_comm_layout(base, self.world, self.max_m, self.hidden)
+            comm.inbox[r], comm.counters[r] = inbox, counters
+            if r == self.rank:
+                comm.epoch = epoch
+        self.comm = comm
+        if self.world > 1:
+            dist.barrier(group=self.group)  # every buffer is zeroed and mapped before any push
+        return comm
+
+    def close_comm(self):
+        """Unmap the peers' buffers (before the process group goes away)."""
+        for base in self._peer_bases:
+            ipc_close(base)
+        self._peer_bases = []
+        self.comm = None
+
+    def _enqueue_fused(self, h, act, workspace):
+        if self.comm is None:
+            raise RuntimeError("fused TPStack needs setup_comm() first")
+        n = self.n_layers
+        for layer in range(n):
+            pgu, sgu, pd, sd = self.layers[layer]
+            if layer == 0:
+                self.gate_up.enqueue(h, pgu, sgu, y=act, workspace=workspace, rms_eps=self.rms_eps, pdl=True,
+                                     prefetch=(self.down, pd))
+            else:
+                # h = sum of the ranks' previous down outputs, summed here
+                self.gate_up.enqueue_tp(self.comm, TP_GATHER, (layer - 1) % 2, h, pgu, sgu, y=act,
+                                        workspace=workspace, rms_eps=self.rms_eps, pdl=True,
+                                        prefetch=(self.down, pd), push_op=self.down, h_out=h)
+            nxt = self.layers[(layer + 1) % n]
+            self.down.enqueue_tp(self.comm, TP_PUSH, layer % 2, act, pd, sd, y=h, workspace=workspace,
+                                 residual=h if self.rank == 0 else None, pdl=True,
+                                 prefetch=None if nxt is None else (self.gate_up, nxt[0]))
+        tp_gather(self.comm, (n - 1) % 2, self.down, h)
         return h

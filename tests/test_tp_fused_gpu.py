@@ -1,0 +1,141 @@
+"""The all-reduce fused into the GEMVs through peer memory (b2g_enqueue_tp).
+
+* world = 1 on one GPU: the push/gather path (inbox slot, arrival counters,
+  epoch, final gather) must give bitwise the rows of the plain path;
+* a wait that nothing satisfies expires (bounded) and reports through the
+  device error word, leaving the rows untouched;
+* two ranks on two GPUs (when the machine has them): rank 0's result
+  against the oracle's sharded restatement.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_b2g, load_oracle, load_synthetic
+
+pytestmark = pytest.mark.gpu
+
+
+def _tp(b2g):
+    return __import__("b2g.tp", fromlist=["TPStack"])
+
+
+def _weights(orc, syn, hidden, inter, n_layers, seed0):
+    out = []
+    for l in range(n_layers):
+        ws = [syn.weights(seed0 + 3 * l + j, K, N)
+              for j, (K, N) in enumerate(((hidden, inter), (hidden, inter), (inter, hidden)))]
+        (qg, sg), (qu, su), (qd, sd) = (orc.quantize_e4m3(w, orc.SCALE_CHANNEL_FP32) for w in ws)
+        out.append({"wg": qg, "wu": qu, "wd": qd, "sg": sg, "su": su, "sd": sd})
+    return out
+
+
+def _load_layers(st, layers, dev):
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    for l, L in enumerate(layers):
+        st.prepack_layer(l, t(L["wg"]), t(L["wu"]), t(L["wd"]), t(L["sg"]), t(L["su"]), t(L["sd"]))
+
+
+@pytest.mark.parametrize("hidden,inter,n_layers", [(256, 512, 3), (3072, 8192, 2)])
+def test_fused_world1_matches_plain(b2g, orc, syn, cuda, hidden, inter, n_layers):
+    tp = _tp(b2g)
+    layers = _weights(orc, syn, hidden, inter, n_layers, 3000)
+    plain = tp.TPStack(hidden, inter, n_layers, rank=0, world=1, max_m=8)
+    fused = tp.TPStack(hidden, inter, n_layers, rank=0, world=1, max_m=8, fused=True)
+    _load_layers(plain, layers, cuda)
+    _load_layers(fused, layers, cuda)
+    fused.setup_comm(cuda)
+    ws_p, ws_f = plain.workspace(cuda), fused.workspace(cuda)
+    for M in (1, 8):
+        h0 = syn.hidden_state(M, hidden)
+        hp = torch.from_numpy(h0).to(cuda)
+        hf = hp.clone()
+        act_p = torch.empty(M, inter, dtype=torch.float16, device=cuda)
+        act_f = act_p.clone()
+        for _ in range(2):  # a second step reuses the inbox buffers and counters
+            plain.enqueue(hp, act_p, ws_p)
+            fused.enqueue(hf, act_f, ws_f)
+        torch.cuda.synchronize()
+        assert torch.equal(hp, hf), M
+        want = orc.mlp_stack(orc.mlp_stack(h0, layers), layers)
+        r = orc.compare(hf.cpu().numpy(), want.astype(np.float64))
+        assert r["rel_l2"] <= 5e-3, r
+    assert b2g.device_error() == 0
+    fused.close_comm()
+
+
+def test_gather_wait_expires(b2g, orc, syn, cuda):
+    """An arrival that never comes: the bounded wait gives up, records the
+    peer-wait code and leaves h as it was."""
+    tp = _tp(b2g)
+    st = tp.TPStack(256, 512, 1, rank=0, world=1, max_m=8, fused=True)
+    comm = st.setup_comm(cuda)
+    _, _, epoch = b2g.tp_comm_layout(st._comm_buf.data_ptr(), 1, 8, 256)
+    off = epoch - st._comm_buf.data_ptr()
+    st._comm_buf[off:off + 4].view(torch.int32).fill_(1)  # one round expected, none pushed
+    h = torch.full((2, 256), 3.0, dtype=torch.float16, device=cuda)
+    b2g.tp_gather(comm, 0, st.down, h)
+    torch.cuda.synchronize()
+    assert b2g.device_error(clear=True) == 4  # peer wait expired
+    assert bool((h == 3.0).all())
+    st.close_comm()
+
+
+# --------------------------------------------------------------------------
+# Two ranks, one GPU each
+# --------------------------------------------------------------------------
+HID, INT, NL, MM = 3072, 8192, 2, 8
+
+
+def _rank(rank, world, port, out):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)  # handle exchange only
+    b2g, orc, syn = load_b2g(), load_oracle(), load_synthetic()
+    tp = __import__("b2g.tp", fromlist=["TPStack"])
+    layers = _weights(orc, syn, HID, INT, NL, 4000)
+    st = tp.TPStack(HID, INT, NL, rank=rank, world=world, max_m=8, fused=True)
+    _load_layers(st, layers, dev)
+    st.setup_comm(dev)
+    h = torch.from_numpy(syn.hidden_state(MM, HID)).to(dev)
+    act = torch.empty(MM, st.shard, dtype=torch.float16, device=dev)
+    st.enqueue(h, act, st.workspace(dev))
+    torch.cuda.synchronize()
+    err = b2g.device_error()
+    dist.barrier()
+    st.close_comm()
+    if rank == 0:
+        np.save(out, h.cpu().numpy())
+        with open(out + ".err", "w") as f:
+            f.write(str(err))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_fused_two_ranks(b2g, orc, syn, cuda, tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "h.npy")
+    mp.spawn(_rank, args=(2, _port(), out), nprocs=2, join=True)
+    got = np.load(out)
+    assert open(out + ".err").read() == "0"
+    layers = _weights(orc, syn, HID, INT, NL, 4000)
+    want = syn.hidden_state(MM, HID)
+    for L in layers:
+        want = orc.mlp_layer_tp(want, L, 2)
+    r = orc.compare(got, want.astype(np.float64))
+    assert r["rel_l2"] <= 5e-3, r
