@@ -446,6 +446,10 @@ def run_ours(args):
 
     plan_gu, plan_dn = gu_op.plan(M), dn_op.plan(M)
     err = b2g.device_error()
+    if world > 1:  # the worst device error over ranks (a peer wait that expired anywhere voids the run)
+        e = torch.tensor([err], dtype=torch.int32, device=device)
+        dist.all_reduce(e, op=dist.ReduceOp.MAX)
+        err = int(e.item())
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world,
@@ -505,6 +509,8 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if err:
+        sys.exit(f"device error {err} recorded during the run: the timing is void")
 
 
 def run_reference(args):

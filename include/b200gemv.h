@@ -245,7 +245,9 @@ b2g_status b2g_enqueue_static(const b2g_op* op, const b2g_enqueue_args* args, b2
  *     h_out (the residual input of the next down op).
  * After the last layer b2g_tp_gather writes the final rows.  Consecutive
  * layers alternate between the inbox's two buffers (`buf`).  A wait that
- * expires sets the device error word (B2G_ERR_PEER_TIMEOUT class, code 4).
+ * expires sets the device error word (B2G_ERR_PEER_TIMEOUT class, code 4);
+ * while the word is set, later waits give up at once (a lost peer costs one
+ * 2 s wait, not one per layer) and skip their writes.
  * ------------------------------------------------------------------------ */
 #define B2G_TP_MAX_RANKS 8
 enum { B2G_TP_NONE = 0, B2G_TP_PUSH = 1, B2G_TP_GATHER = 2 };

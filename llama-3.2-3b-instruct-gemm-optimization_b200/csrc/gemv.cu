@@ -369,6 +369,7 @@ __device__ void stage_x(const GemvParams& p, const Io& io, __half* xs, int k_lo,
 // epoch * push_grid: every rank's pushing launch of this round has finished
 // its stores.  Counters only grow; the comparison tolerates wrap-around.
 __device__ __forceinline__ bool tp_wait_arrivals(const TpParams& tp, int* err) {
+  if (*reinterpret_cast<volatile int*>(err) != 0) return false;  // an earlier wait failed: fail fast
   const unsigned target = *reinterpret_cast<volatile unsigned*>(tp.epoch) * (unsigned)tp.push_grid;
   const unsigned* cnt = tp.counters[tp.rank];
   const unsigned long long t0 = globaltimer_ns();

@@ -4,13 +4,15 @@
   epoch, final gather) must give bitwise the rows of the plain path;
 * a wait that nothing satisfies expires (bounded) and reports through the
   device error word, leaving the rows untouched;
-* two ranks on two GPUs (when the machine has them): rank 0's result
-  against the oracle's sharded restatement.
+* two ranks on two GPUs, and every GPU of the machine (up to 8) when it
+  has more: rank 0's result against the oracle's sharded restatement, every
+  rank's rows bitwise equal.
 """
 from __future__ import annotations
 
 import os
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -81,7 +83,14 @@ def test_gather_wait_expires(b2g, orc, syn, cuda):
     h = torch.full((2, 256), 3.0, dtype=torch.float16, device=cuda)
     b2g.tp_gather(comm, 0, st.down, h)
     torch.cuda.synchronize()
-    assert b2g.device_error(clear=True) == 4  # peer wait expired
+    assert b2g.device_error(clear=False) == 4  # peer wait expired
+    assert bool((h == 3.0).all())
+    # while the error word is set, a later wait gives up at once
+    t0 = time.perf_counter()
+    b2g.tp_gather(comm, 0, st.down, h)
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 0.5
+    assert b2g.device_error(clear=True) == 4
     assert bool((h == 3.0).all())
     st.close_comm()
 
@@ -111,10 +120,9 @@ def _rank(rank, world, port, out):
     err = b2g.device_error()
     dist.barrier()
     st.close_comm()
-    if rank == 0:
-        np.save(out, h.cpu().numpy())
-        with open(out + ".err", "w") as f:
-            f.write(str(err))
+    np.save(out + f".{rank}.npy", h.cpu().numpy())
+    with open(out + f".{rank}.err", "w") as f:
+        f.write(str(err))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -125,17 +133,22 @@ def _port():
         return s.getsockname()[1]
 
 
-def test_fused_two_ranks(b2g, orc, syn, cuda, tmp_path):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+@pytest.mark.parametrize("which", ["two", "all"])
+def test_fused_ranks(b2g, orc, syn, cuda, tmp_path, which):
+    n = min(torch.cuda.device_count(), 8)
+    if n < 2 or (which == "all" and n == 2):
+        pytest.skip("needs two GPUs" if n < 2 else "all = two here")
+    world = 2 if which == "two" else n
     import torch.multiprocessing as mp
-    out = str(tmp_path / "h.npy")
-    mp.spawn(_rank, args=(2, _port(), out), nprocs=2, join=True)
-    got = np.load(out)
-    assert open(out + ".err").read() == "0"
+    out = str(tmp_path / "h")
+    mp.spawn(_rank, args=(world, _port(), out), nprocs=world, join=True)
+    got = [np.load(out + f".{r}.npy") for r in range(world)]
+    assert [open(out + f".{r}.err").read() for r in range(world)] == ["0"] * world
+    for r in range(1, world):
+        assert np.array_equal(got[r], got[0]), r  # the same sum, in the same order, on every rank
     layers = _weights(orc, syn, HID, INT, NL, 4000)
     want = syn.hidden_state(MM, HID)
     for L in layers:
-        want = orc.mlp_layer_tp(want, L, 2)
-    r = orc.compare(got, want.astype(np.float64))
+        want = orc.mlp_layer_tp(want, L, world)
+    r = orc.compare(got[0], want.astype(np.float64))
     assert r["rel_l2"] <= 5e-3, r
