@@ -55,6 +55,14 @@ std::mutex g_mu;
 bool g_limit_set[64];
 int* g_err_word[64];
 
+// L2 prefetch depth: the first bytes of each next-launch CTA's range that a
+// launch warms (the start is what the next CTA's register ring asks for
+// first; warming whole ranges moves more of the next launch's HBM traffic
+// into this launch's window).  Per decode layer (gate||up on 128 CTAs, down
+// on 96): 64 KB 26.2 us, 128 KB 26.5, 256 KB 25.9, whole ranges 26.1 at
+// M = 8; 25.3 / 25.7 / 24.4 / 24.5 at M = 1.
+constexpr int kPrefetchBytesPerCta = 256 * 1024;
+
 b2g_status ensure_device_setup(int dev, int smem_optin) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (dev < 0 || dev >= 64) return B2G_ERR_UNSUPPORTED;
@@ -146,10 +154,14 @@ b2g_status replan(b2g_op* op) {
   bool aligned = op->partition == B2G_PARTITION_TILES;
   if (op->partition == B2G_PARTITION_AUTO) {
     // Whole virtual tiles per CTA remove the cross-CTA handshake of split
-    // tiles; take that when nothing is split along K anyway and the
-    // granularity costs at most ~20% of stream imbalance.
+    // tiles, and the SMs the shrunk grid leaves idle take the next launch's
+    // CTAs early (programmatic dependent launch), which start their weight
+    // stream there.  Taken when nothing is split along K anyway and the
+    // largest share is at most 1.6x the even share: down 8192->3072 (192
+    // tiles, 2 per CTA on 96 CTAs against 1.3 on 148) measured 10.6 vs
+    // 11.0 us per launch and 25.6 vs 27.2 us per decode layer.
     const long long g = std::min<long long>(n_vt, want);
-    aligned = op->ksplit == 1 && (double)((n_vt + g - 1) / g) / ((double)n_vt / g) <= 1.2;
+    aligned = op->ksplit == 1 && (double)((n_vt + g - 1) / g) / ((double)n_vt / g) <= 1.6;
   }
   op->gran = aligned ? op->kbpv : 1;
   op->total_gran = op->total_units / op->gran;
@@ -446,7 +458,7 @@ static b2g_status enqueue_impl(const b2g_op* op, const b2g_enqueue_args* a, cons
     p.pf_gran = nx->gran;
     p.pf_unit_bytes = nx->unit_bytes;
     p.pf_grid = nx->grid;
-    p.pf_bytes = 1 << 30;  // the CTA's whole range
+    p.pf_bytes = kPrefetchBytesPerCta;
   }
   if (tp) p.tp = *tp;
   return cuda_status(launch_gemv(p, op->planes, op->wbytes, op->math, lp.smem, a->pdl != 0,

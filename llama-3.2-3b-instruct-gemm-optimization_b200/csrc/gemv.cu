@@ -838,16 +838,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_
   // Weights are constant: the first loads go out before the previous kernel
   // in the stream is waited on.
   prefetch_phase<P, R>(p, p.packed, ring, warp, lane, pol);
-  // Warm L2 with the range the next kernel's CTA of the same index will
-  // stream, so HBM keeps working through this kernel's tail and the launch gap.
-  if (tid == 0 && p.pf_packed != nullptr && (int)blockIdx.x < p.pf_grid) {
+  // Warm L2 with the start of the ranges the next kernel's CTAs will stream
+  // (next CTAs blockIdx.x, blockIdx.x + grid, ...), so HBM keeps working
+  // through this kernel's tail and the launch gap, and the next kernel's
+  // first loads hit L2.
+  if (tid == 0 && p.pf_packed != nullptr) {
     const long long tg = p.pf_total_units / p.pf_gran;
-    const long long a = (long long)blockIdx.x * tg / p.pf_grid * p.pf_gran;
-    const long long b = (long long)(blockIdx.x + 1) * tg / p.pf_grid * p.pf_gran;
-    const long long bytes = min((long long)p.pf_bytes, (b - a) * p.pf_unit_bytes);
-    const uint8_t* src = p.pf_packed + a * p.pf_unit_bytes;
-    for (long long off = 0; off < bytes; off += 32768)
-      bulk_prefetch_l2(src + off, (uint32_t)min(32768LL, bytes - off));
+    for (int c = blockIdx.x; c < p.pf_grid; c += p.grid) {
+      const long long a = (long long)c * tg / p.pf_grid * p.pf_gran;
+      const long long b = (long long)(c + 1) * tg / p.pf_grid * p.pf_gran;
+      const long long bytes = min((long long)p.pf_bytes, (b - a) * p.pf_unit_bytes);
+      const uint8_t* src = p.pf_packed + a * p.pf_unit_bytes;
+      for (long long off = 0; off < bytes; off += 32768)
+        bulk_prefetch_l2(src + off, (uint32_t)min(32768LL, bytes - off));
+    }
   }
   pdl_launch_dependents();
   pdl_wait();

@@ -114,8 +114,10 @@ struct GemvParams {
   int off_epi;    // shared-memory byte offset of the epilogue inputs
   int off_x;      // shared-memory byte offset of the x rows
   int x_rs;       // x row stride in shared memory (halves)
-  // L2 prefetch of the next kernel's stream: CTA c prefetches the first
-  // pf_bytes of the range the next kernel's CTA c will stream (0 = off).
+  // L2 prefetch of the next kernel's stream (pf_packed null = off): the
+  // first pf_bytes of every range the next launch's CTAs will stream (its
+  // partition: pf_total_units units of pf_unit_bytes in granules of pf_gran
+  // over pf_grid CTAs); this launch's CTA c takes the next CTAs c, c + grid, ...
   const uint8_t* pf_packed;
   long long pf_total_units;
   int pf_gran;
