@@ -172,8 +172,10 @@ __device__ __forceinline__ float rms_of(const GemvParams& p, const float* red, i
 
 // red: RMSNorm partial sums (nullptr when the op has no RMSNorm); the
 // normalisation is linear, so it scales the accumulator: y = fp16(acc * r_m * s_n).
-// stage: 256 B of this warp's own shared memory, for PUSH rows.
-template <int P>
+// stage: 256 B of this warp's own shared memory, for PUSH rows.  TPX: the
+// launch may exchange rows with other ranks (the TP code is compiled only
+// into those kernels).
+template <int P, bool TPX>
 __device__ __forceinline__ void epilogue(const GemvParams& p, const Io& io, int j, int tile, const float (&v)[P][4],
                                          int lane, const float* red, const Epi& e, __half* stage) {
   const int g = lane >> 2, q = lane & 3;
@@ -196,13 +198,13 @@ __device__ __forceinline__ void epilogue(const GemvParams& p, const Io& io, int 
         const float uf = __half2float(__float2half_rn(v[1][i] * r * e.scale[(j * 2 + 1) * 16 + c]));
         out = __float2half_rn(gf / (1.0f + __expf(-gf)) * uf);
       }
-      if (P == 1 && p.tp.mode == kTpPush)
+      if (TPX && P == 1 && p.tp.mode == kTpPush)
         stage[m * 16 + c] = out;
       else
         io.y[(size_t)m * io.ldy + n] = out;
     }
   }
-  if (P == 1 && p.tp.mode == kTpPush) {
+  if (TPX && P == 1 && p.tp.mode == kTpPush) {
     // The tile's rows are 32 B each: two lanes per row store 16 B into this
     // rank's slot of every rank's inbox (peer stores over NVLink).
     __syncwarp();
@@ -219,7 +221,7 @@ __device__ __forceinline__ void epilogue(const GemvParams& p, const Io& io, int 
 // A virtual tile's CTA-level sum is complete in v: finish it here if this CTA
 // is the tile's only contributor, else publish it and let the last
 // contributing CTA sum all partials in (k-range, CTA) order.
-template <int P>
+template <int P, bool TPX>
 __device__ __forceinline__ void finish_vt(const GemvParams& p, const Io& io, int vt, int j, const float (&v)[P][4],
                                           int lane, const float* red, const Epi& e, __half* stage) {
   const int ks = fdiv(vt, p.div_tiles);
@@ -285,7 +287,7 @@ __device__ __forceinline__ void finish_vt(const GemvParams& p, const Io& io, int
     }
     if (lane == 0) p.counters[tile] = 0;
   }
-  epilogue<P>(p, io, j, tile, s, lane, red, e, stage);
+  epilogue<P, TPX>(p, io, j, tile, s, lane, red, e, stage);
 }
 
 // Sum of squares of 8 halves, in one fixed order (stage_x and gather_x share
@@ -813,7 +815,7 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
     }
     // slot j's shared memory is this warp's alone once summed: the PUSH stage
     __syncwarp();
-    finish_vt<P>(p, io, vt_first + j, j, v, lane, p.rmsnorm ? red : nullptr, epi,
+    finish_vt<P, TP>(p, io, vt_first + j, j, v, lane, p.rmsnorm ? red : nullptr, epi,
                  reinterpret_cast<__half*>(slots + (size_t)j * W * P * 32));
   }
 #ifdef B2G_TRACE
@@ -825,7 +827,7 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
 // ---------------------------------------------------------------------------
 // One GEMV per launch
 // ---------------------------------------------------------------------------
-template <int P, int WB, int MATH>
+template <int P, int WB, int MATH, bool TPX>
 __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   // 128 KB of weights in flight per SM (16 B x 512 threads x 16); the FFMA
@@ -856,9 +858,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_
   pdl_launch_dependents();
   pdl_wait();
   if (tid == 0) TRACE(1);
-  if (p.tp.mode == kTpPush && blockIdx.x == 0 && tid == 0) atomicAdd(p.tp.epoch, 1u);
-  run_phase<P, WB, MATH, R, NoHook, true>(p, io_of_params(p), smem, ring, pol, NoHook{});
-  if (p.tp.mode == kTpPush) {
+  if (TPX && p.tp.mode == kTpPush && blockIdx.x == 0 && tid == 0) atomicAdd(p.tp.epoch, 1u);
+  run_phase<P, WB, MATH, R, NoHook, TPX>(p, io_of_params(p), smem, ring, pol, NoHook{});
+  if (TPX && p.tp.mode == kTpPush) {
     // This CTA's peer stores are done: one arrival on every rank.
     __syncthreads();
     if (tid == 0) {
@@ -969,7 +971,8 @@ cudaError_t launch_variant(const GemvParams& p, size_t smem, bool pdl, cudaStrea
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH>, p);
+  if (p.tp.mode != kTpNone) return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, true>, p);
+  return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, false>, p);
 }
 
 }  // namespace
@@ -1049,14 +1052,22 @@ cudaError_t gemv_set_smem_limit(int bytes) {
   cudaError_t e = cudaSuccess, r;
 #define B2G_LIM(K) \
   if ((r = cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes)) != cudaSuccess) e = r;
-  B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma>))
-  B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma>))
-  B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma>))
-  B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma>))
-  B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma>))
-  B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma>))
-  B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma>))
-  B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, false>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, true>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma, false>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma, true>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, false>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, true>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma, false>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma, true>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, false>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, true>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma, false>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma, true>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma, false>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma, true>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma, false>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma, true>))
   B2G_LIM((stack_kernel<1>))
   B2G_LIM((stack_kernel<2>))
 #undef B2G_LIM
