@@ -405,7 +405,7 @@ def run_ours(args):
     tf = ROOT / "profiles" / "traffic.json"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(f"gate_up_m{M}_tp{tp}")
-    roofline = {"kernel": "gemv_streamk_kernel<2,1,0> (RMSNorm + gate||up + SiLU*up)",
+    roofline = {"kernel": "gemv_streamk_kernel<2,1,0,1> (RMSNorm + gate||up + SiLU*up)",
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "traffic": traffic,
                 "peak_source": f"{peak_kind} hbm_gbs (STREAM-style copy)",
