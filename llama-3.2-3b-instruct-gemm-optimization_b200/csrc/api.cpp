@@ -148,9 +148,11 @@ bool plan_launch(const b2g_op* op, int m, LaunchPlan* lp) {
   return lp->smem <= (size_t)op->smem_optin;
 }
 
-b2g_status replan(b2g_op* op) {
+// One planning pass for `want` CTAs.  *slots_full: the CTAs' ranges touch
+// more virtual tiles than their shared slots hold.
+b2g_status plan_at(b2g_op* op, long long want, bool* slots_full) {
+  *slots_full = false;
   const long long n_vt = (long long)op->ksplit * op->n_tiles;
-  const int want = op->grid_override > 0 ? op->grid_override : op->num_sms;
   bool aligned = op->partition == B2G_PARTITION_TILES;
   if (op->partition == B2G_PARTITION_AUTO) {
     // Whole virtual tiles per CTA remove the cross-CTA handshake of split
@@ -175,10 +177,28 @@ b2g_status replan(b2g_op* op) {
   // The kernels' partition arithmetic is 32-bit.
   if ((op->total_gran + 2) * (long long)op->grid >= (1LL << 31)) return B2G_ERR_UNSUPPORTED;
   plan_partition(op);
-  if (op->n_slots > kMaxSlots) return B2G_ERR_UNSUPPORTED;
+  if (op->n_slots > kMaxSlots) {
+    *slots_full = true;
+    return B2G_ERR_UNSUPPORTED;
+  }
   LaunchPlan lp;
   if (!plan_launch(op, op->f.max_m, &lp)) return B2G_ERR_OOM;
   return B2G_OK;
+}
+
+b2g_status replan(b2g_op* op) {
+  bool slots_full = false;
+  if (op->grid_override > 0) return plan_at(op, op->grid_override, &slots_full);
+  // One CTA per SM; or, when that hands a CTA more virtual tiles than its
+  // shared slots hold (very wide outputs, e.g. a 3072 -> 128256 vocabulary
+  // projection: 8016 tiles), the CTAs that keep each range within
+  // kMaxSlots - 1 whole tiles (a split range touches one more), run as
+  // successive waves.
+  b2g_status st = plan_at(op, op->num_sms, &slots_full);
+  const long long n_vt = (long long)op->ksplit * op->n_tiles;
+  long long want = (n_vt + kMaxSlots - 2) / (kMaxSlots - 1);
+  for (int i = 0; slots_full && i < 8; ++i, want += want / 4 + 1) st = plan_at(op, want, &slots_full);
+  return st;
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }

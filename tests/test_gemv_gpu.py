@@ -97,6 +97,49 @@ def test_gemv_parity(b2g, orc, syn, cuda, K, N, wd, mode):
         check(orc, y, want, wd, (K, N, M))
 
 
+# The adjacent decode projections of the same model, on the same kernels:
+# qkv_proj 3072 -> 5120 (320 tiles) and o_proj 3072 -> 3072 (192 tiles).
+@pytest.mark.parametrize("K,N", [(3072, 5120), (3072, 3072)])
+@pytest.mark.parametrize("wd,mode", [(1, 3), (0, 0)])
+def test_adjacent_decode_projections(b2g, orc, syn, cuda, K, N, wd, mode):
+    Wd, Wh, s = make_weights(orc, syn, 41, K, N, wd, mode)
+    for M in (1, 8):
+        x = syn.activations(500 + M, M, K)
+        _, _, y = run_op(b2g, K, N, wd, mode, dev(x), Wd, s)
+        want = orc.gemv(Wh, orc.WTYPE_FP8 if wd else orc.WTYPE_FP16, x, mode, s)
+        check(orc, y, want, wd, (K, N, M))
+
+
+def test_vocab_projection_in_waves(b2g, orc, cuda):
+    """lm_head 3072 -> 128256 (8016 tiles): more tiles per CTA than its shared
+    slots hold at one CTA per SM, so the planner launches more CTAs, run as
+    successive waves.  Weights are drawn on the device (394 M of them) and
+    quantised there (bit-exact against the oracle elsewhere); the output is
+    checked against the oracle on column blocks at both ends and the middle."""
+    K, N = 3072, 128256
+    g = torch.Generator(device=cuda).manual_seed(55)
+    W = (torch.randn(K, N, generator=g, device=cuda) * 0.02).half()
+    q, s = b2g.quantize_e4m3(W, "channel_fp32")
+    del W
+    op = b2g.GemvOp(K, N, weight_dtype=1, scale_mode="channel_fp32", max_m=8)
+    plan = op.plan(8)
+    assert plan["n_slots"] <= 8 and plan["grid"] * plan["n_slots"] >= plan["n_tiles"], plan
+    packed = op.prepack(q)
+    qh, sh = host(q), host(s)
+    rng = np.random.default_rng(56)
+    for M in (1, 8):
+        x = rng.standard_normal((M, K), dtype=np.float32).astype(np.float16)
+        y = host(op.enqueue(dev(x), packed, s))
+        for lo in (0, N // 2 - 2048, N - 4096):
+            cols = slice(lo, lo + 4096)
+            want = orc.gemv(np.ascontiguousarray(qh[:, cols]), orc.WTYPE_FP8, x, orc.SCALE_CHANNEL_FP32,
+                            np.ascontiguousarray(sh[cols]))
+            r = orc.compare(y[:, cols], want)
+            assert r["rel_l2"] <= TOL[1], (M, lo, r)
+            assert r["max_abs"] <= MAX_ABS[1] * max(1.0, np.abs(want).max() / 4), (M, lo, r)
+    assert b2g.device_error() == 0
+
+
 @pytest.mark.parametrize("K,N", [(3072, 8192), (200, 120)])
 def test_gemv_nk_layout(b2g, orc, syn, cuda, K, N):
     for wd in (0, 1):
