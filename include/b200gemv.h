@@ -164,6 +164,14 @@ typedef struct {
   int32_t math;
 } b2g_plan_info;
 b2g_status b2g_op_query(const b2g_op* op, int32_t m, b2g_plan_info* info);
+/* The plan b2g_create would make on a GPU with num_sms SMs and smem_optin
+ * bytes of opt-in shared memory per block, made without touching a device
+ * (build-time sizing, e.g. IPluginV3OneBuild::getWorkspaceSize on a machine
+ * without the target GPU; planner tests).  Also returns the packed-weight and
+ * workspace bytes for m rows (either pointer may be NULL).  B200: 148 SMs,
+ * 232448 bytes. */
+b2g_status b2g_plan_for_device(const b2g_fields* f, int32_t num_sms, int32_t smem_optin, int32_t m,
+                               b2g_plan_info* info, size_t* packed_bytes, size_t* workspace_bytes);
 
 /* Bytes of the pre-packed weight buffer.  (The reference streams the raw
  * [K, N] bytes, kernels/gemv_fp8.cu:93; the library streams a tile layout.) */

@@ -92,6 +92,8 @@ SIGNATURES = {
     "b2g_destroy": ([_P], ctypes.c_int),
     "b2g_op_set_option": ([_P, _I32, _I32], ctypes.c_int),
     "b2g_op_query": ([_P, _I32, ctypes.POINTER(PlanInfo)], ctypes.c_int),
+    "b2g_plan_for_device": ([ctypes.POINTER(Fields), _I32, _I32, _I32, ctypes.POINTER(PlanInfo),
+                             ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)], ctypes.c_int),
     "b2g_prepack_size": ([_P, ctypes.POINTER(_SZ)], ctypes.c_int),
     "b2g_prepack": ([_P, _P, _P, _I64, _P, _P], ctypes.c_int),
     "b2g_quantize_e4m3": ([_P, _I32, _I32, _I32, _I32, _P, _P, _P], ctypes.c_int),
@@ -284,6 +286,24 @@ class GemvOp:
                         _rows_stride(y), None, rms_eps, 0, None, None)
         check(lib().b2g_enqueue_static(self.h, ctypes.byref(a), _stream(stream)), "b2g_enqueue_static")
         return y
+
+
+B200_SMS, B200_SMEM_OPTIN = 148, 232448
+
+
+def plan_for_device(in_features: int, out_features: int, weight_dtype="fp8_e4m3", scale_mode="channel_fp32",
+                    layout="KN", max_m: int = 8, fuse: int = FUSE_NONE, m=None, num_sms: int = B200_SMS,
+                    smem_optin: int = B200_SMEM_OPTIN) -> dict:
+    """The plan GemvOp would make on a GPU with num_sms SMs (b2g_plan_for_device;
+    no device needed), with its packed-weight and workspace bytes."""
+    f = Fields(in_features, out_features, _code(DTYPE, weight_dtype), _code(SCALE, scale_mode),
+               _code(LAYOUT, layout), max_m, fuse, 0, 1)
+    info, pb, wb = PlanInfo(), ctypes.c_size_t(), ctypes.c_size_t()
+    check(lib().b2g_plan_for_device(ctypes.byref(f), num_sms, smem_optin, m or max_m, ctypes.byref(info),
+                                    ctypes.byref(pb), ctypes.byref(wb)), "b2g_plan_for_device")
+    d = info.as_dict()
+    d.update(packed_bytes=pb.value, workspace_bytes=wb.value)
+    return d
 
 
 def quantize_e4m3(w16, scale_mode="channel_fp32", layout="KN", stream=None):

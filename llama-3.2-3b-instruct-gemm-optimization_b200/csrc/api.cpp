@@ -254,8 +254,11 @@ const char* b2g_status_string(b2g_status s) {
 
 int32_t b2g_version(void) { return 100; }
 
-b2g_status b2g_create(const b2g_fields* f, b2g_op** out) {
-  if (!f || !out) return B2G_ERR_INVALID;
+namespace {
+
+// A new op with the fields checked and the derived sizes set (no device
+// attributes yet, no plan).
+b2g_status new_op(const b2g_fields* f, b2g_op** out) {
   *out = nullptr;
   if (f->in_features <= 0 || f->out_features <= 0) return B2G_ERR_INVALID;
   if (f->weight_dtype != B2G_DTYPE_FP16 && f->weight_dtype != B2G_DTYPE_FP8_E4M3) return B2G_ERR_INVALID;
@@ -279,11 +282,7 @@ b2g_status b2g_create(const b2g_fields* f, b2g_op** out) {
   op->Kp = (op->K + 31) / 32 * 32;
   op->kb_total = op->Kp / op->kpb;
   op->n_tiles = (op->N + kTileCh - 1) / kTileCh;
-  if (op->n_tiles > kMaxTiles) {
-    delete op;
-    return B2G_ERR_UNSUPPORTED;
-  }
-  if ((f->fuse & B2G_FUSE_RMSNORM_INPUT) && (op->K % 8) != 0) {
+  if (op->n_tiles > kMaxTiles || ((f->fuse & B2G_FUSE_RMSNORM_INPUT) && (op->K % 8) != 0)) {
     delete op;
     return B2G_ERR_UNSUPPORTED;
   }
@@ -297,7 +296,20 @@ b2g_status b2g_create(const b2g_fields* f, b2g_op** out) {
   op->unit_bytes = op->planes * kUnitPlaneBytes;
   op->packed_bytes = (size_t)op->total_units * op->unit_bytes;
   op->math = kMathMma;
+  *out = op;
+  return B2G_OK;
+}
 
+}  // namespace
+
+b2g_status b2g_create(const b2g_fields* f, b2g_op** out) {
+  if (!f || !out) return B2G_ERR_INVALID;
+  b2g_op* op = nullptr;
+  b2g_status st = new_op(f, &op);
+  if (st != B2G_OK) {
+    *out = nullptr;
+    return st;
+  }
   cudaError_t e = cudaGetDevice(&op->device);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&op->num_sms, cudaDevAttrMultiProcessorCount, op->device);
   if (e == cudaSuccess)
@@ -308,13 +320,31 @@ b2g_status b2g_create(const b2g_fields* f, b2g_op** out) {
     delete op;
     return B2G_ERR_CUDA;
   }
-  b2g_status st = replan(op);
+  st = replan(op);
   if (st != B2G_OK) {
     delete op;
     return st;
   }
   *out = op;
   return B2G_OK;
+}
+
+b2g_status b2g_plan_for_device(const b2g_fields* f, int32_t num_sms, int32_t smem_optin, int32_t m,
+                               b2g_plan_info* info, size_t* packed_bytes, size_t* workspace_bytes) {
+  if (!f || !info || num_sms < 1 || smem_optin < 1) return B2G_ERR_INVALID;
+  b2g_op* op = nullptr;
+  b2g_status st = new_op(f, &op);
+  if (st != B2G_OK) return st;
+  op->device = -1;
+  op->num_sms = num_sms;
+  op->smem_optin = smem_optin;
+  op->smem_per_sm = smem_optin;
+  st = replan(op);
+  if (st == B2G_OK) st = b2g_op_query(op, m, info);
+  if (st == B2G_OK && packed_bytes) st = b2g_prepack_size(op, packed_bytes);
+  if (st == B2G_OK && workspace_bytes) st = b2g_workspace_size(op, m, workspace_bytes);
+  delete op;
+  return st;
 }
 
 b2g_status b2g_destroy(b2g_op* op) {
@@ -369,7 +399,7 @@ b2g_status b2g_op_query(const b2g_op* op, int32_t m, b2g_plan_info* info) {
   info->n_tiles = op->n_tiles;
   info->total_units = op->total_units;
   info->unit_bytes = op->unit_bytes;
-  info->inflight_bytes_per_cta = (int64_t)kThreads * 16 * (op->planes == 1 ? 16 : 16);
+  info->inflight_bytes_per_cta = (int64_t)kThreads * 16 * kRing;  // 16 B x kRing per thread, any plane count
   info->smem_bytes = (int64_t)lp.smem;
   info->max_contrib = op->max_contrib;
   info->partition = op->gran == 1 ? B2G_PARTITION_UNITS : B2G_PARTITION_TILES;

@@ -71,7 +71,6 @@ namespace {
 
 constexpr int W = kWarps;
 constexpr int NT = kThreads;
-constexpr int kRing = 16;  // uint4 registers per lane for in-flight weight units
 
 // The buffers one GEMV phase reads and writes.
 struct Io {

@@ -22,6 +22,7 @@ constexpr int kTileCh = 16;
 constexpr int kWarps = 16;  // one CTA of 16 warps per SM
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxSlots = 8;  // virtual tiles one CTA may touch
+constexpr int kRing = 16;     // uint4 registers per lane for in-flight weight units
 // Shared memory: [64,68) barrier verdict, [128,640) RMSNorm sums of squares
 // [16 warps][8 rows], then the per-warp partial slots
 // [n_slots][warps][planes][32 lanes][16 B], then the per-slot epilogue inputs
