@@ -141,6 +141,54 @@ def make_layers(b2g, torch, device, tp: int, rank: int, ops, M: int, keep_raw: b
 
 
 # ---------------------------------------------------------------------------
+# The model's other decode projections on the same op
+# ---------------------------------------------------------------------------
+ADJACENT = (("qkv_proj", 3072, 5120), ("o_proj", 3072, 3072), ("lm_head", 3072, 128256))
+
+
+def adjacent_shapes(b2g, torch, device, M: int, reps: int = 5) -> dict:
+    """qkv_proj, o_proj and lm_head of Llama-3.2-3B (E4M3, per-channel FP32
+    scales, M rows): per-launch time and algorithmic bandwidth, each launch
+    on its own copy of the weights (copies > 256 MB in total, so HBM-fed),
+    chained with PDL and the L2 prefetch of the next launch as in the step."""
+    out = {}
+    for name, K, N in ADJACENT:
+        op = b2g.GemvOp(K, N, max_m=8)
+        g = torch.Generator(device=device)
+        g.manual_seed(77)
+        W = (torch.randn(K, N, generator=g, device=device, dtype=torch.float32) * 0.02).half()
+        q, s = b2g.quantize_e4m3(W, "channel_fp32")
+        del W
+        base = op.prepack(q)
+        del q
+        copies = max(2, -(-(256 << 20) // base.numel()))
+        packs = [base] + [base.clone() for _ in range(copies - 1)]
+        x = torch.randn(M, K, generator=g, device=device, dtype=torch.float32).half()
+        y = torch.empty(M, N, dtype=torch.float16, device=device)
+        ws = op.workspace(device)
+
+        def sweep():
+            for i, p in enumerate(packs):
+                op.enqueue(x, p, s, y=y, workspace=ws, pdl=True, prefetch=(op, packs[(i + 1) % len(packs)]))
+        for _ in range(3):
+            sweep()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            sweep()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * len(packs))
+        alg = op.packed_bytes() + 4 * N + 2 * M * K + 2 * M * N
+        out[name] = {"K": K, "N": N, "m": M, "us_per_launch": round(us, 3), "alg_bytes": alg,
+                     "achieved_gbs": round(alg / us / 1e3, 1), "grid": op.plan(M)["grid"],
+                     "launches_timed": reps * len(packs)}
+        del packs, base
+    return out
+
+
+# ---------------------------------------------------------------------------
 # The reference's own GPU kernels (kernels/gemv_fp8.cu run_gemv, compiled for
 # sm_100a by baseline/Makefile) on the same weights
 # ---------------------------------------------------------------------------
@@ -438,6 +486,15 @@ def run_ours(args):
     if tp == 1 and not args.no_ref_kernels:
         ref_k = reference_kernels(torch, layers, h0, M, ms_step)
 
+    # ---- the model's other decode projections (one GPU; recorded, not fatal:
+    # the step's numbers above stand whatever happens here)
+    adj = None
+    if tp == 1 and not args.no_adjacent:
+        try:
+            adj = adjacent_shapes(b2g, torch, device, M)
+        except Exception as e:
+            adj = {"error": f"{type(e).__name__}: {e}"}
+
     # ---- CPU baseline (rank 0 at N=1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -482,6 +539,7 @@ def run_ours(args):
             "detail": {
                 **detail_extra,
                 "reference_kernels_sm100": ref_k,
+                "adjacent_decode_projections": adj,
                 "direct_launch_ms_per_step": round(ms_direct / args.steps, 5),
                 "gate_up_us_per_launch": round(ms_gu * 1e3, 3),
                 "gate_up_alg_bytes": gu_b,
@@ -560,6 +618,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ref-kernels", action="store_true", help="skip timing the reference's GPU kernels")
+    ap.add_argument("--no-adjacent", action="store_true", help="skip timing qkv_proj / o_proj / lm_head")
     ap.add_argument("--tp-mode", choices=["fused", "nccl"], default="fused",
                     help="N > 1: all-reduce fused into the GEMVs over peer memory, or NCCL")
     ap.add_argument("--layers", type=int, default=LAYERS,
