@@ -106,3 +106,47 @@ def test_tp_stack_two_gloo_ranks(b2g, orc, syn, tmp_path):
     assert r["rel_l2"] <= 2e-3, r
     r_full = orc.compare(got, orc.mlp_stack(h0, layers).astype(np.float64))
     assert r_full["rel_l2"] <= 5e-3, r_full
+
+
+def test_fused_exchange_schedule(b2g, monkeypatch):
+    """TPStack(fused=True)'s launch order on one rank, with recording stand-ins
+    for the ops: layer 0 stages h plainly; every later gate||up gathers the
+    previous layer's pushes from buffer (l - 1) % 2 (and writes h); every down
+    pushes into buffer l % 2, with the residual on rank 0 only; one final
+    gather reads buffer (n - 1) % 2.  Each launch prefetches the next one's
+    weights."""
+    tp_mod = __import__("b2g.tp", fromlist=["TPStack"])
+    calls = []
+
+    class Rec:
+        def __init__(self, name):
+            self.name = name
+
+        def enqueue(self, x, packed, scales=None, **kw):
+            calls.append((self.name, "plain", None, packed, kw.get("prefetch")[1]))
+
+        def enqueue_tp(self, comm, mode, buf, x, packed, scales=None, **kw):
+            assert comm is st.comm
+            if mode == tp_mod.TP_GATHER:
+                assert kw["push_op"] is st.down and kw["h_out"] is h
+            else:
+                assert kw["residual"] is (h if st.rank == 0 else None) and kw["y"] is h
+            pf = kw.get("prefetch")
+            calls.append((self.name, mode, buf, packed, None if pf is None else pf[1]))
+
+    monkeypatch.setattr(tp_mod, "tp_gather", lambda comm, buf, op, hh: calls.append(("final", "gather", buf, None, None)))
+    G, Pu = tp_mod.TP_GATHER, tp_mod.TP_PUSH
+    for rank in (0, 1):
+        calls.clear()
+        st = tp_mod.TPStack(64, 128, 3, rank=rank, world=2, build_ops=False, fused=True)
+        st.gate_up, st.down = Rec("gu"), Rec("dn")
+        st.layers = [(f"pgu{l}", f"sgu{l}", f"pd{l}", f"sd{l}") for l in range(3)]
+        h, act = torch.zeros(4, 64, dtype=torch.float16), torch.zeros(4, 64, dtype=torch.float16)
+        with pytest.raises(RuntimeError, match="setup_comm"):
+            st.enqueue(h, act, None)
+        st.comm = object()
+        st.enqueue(h, act, None)
+        assert calls == [("gu", "plain", None, "pgu0", "pd0"), ("dn", Pu, 0, "pd0", "pgu1"),
+                         ("gu", G, 0, "pgu1", "pd1"), ("dn", Pu, 1, "pd1", "pgu2"),
+                         ("gu", G, 1, "pgu2", "pd2"), ("dn", Pu, 0, "pd2", "pgu0"),
+                         ("final", "gather", 0, None, None)], rank
