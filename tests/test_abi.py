@@ -93,3 +93,43 @@ def test_refused_option_keeps_plan(b2g):
     an invalid key or value is refused before any CUDA call."""
     L = b2g.lib()
     assert L.b2g_op_set_option(None, b2g.OPT_GRID, 0) == b2g.ERR_INVALID
+
+
+def test_header_is_plain_c_and_plans_without_a_device(b2g, tmp_path):
+    """A C11 consumer (what a cgo / JNI / N-API binding compiles against):
+    the header compiles with warnings as errors, every entry point links, and
+    the device-free calls run -- the decode shapes' plans for a B200."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    refs = ",\n    ".join(f"(void (*)(void))&{f}" for f in declared_functions())
+    src = tmp_path / "consumer.c"
+    src.write_text(f"""#include <stdio.h>
+#include "b200gemv.h"
+static void (*const every_entry[])(void) = {{
+    {refs}
+}};
+static int plan(int K, int N, int fuse) {{
+  b2g_fields f = {{K, N, B2G_DTYPE_FP8_E4M3, B2G_SCALE_CHANNEL_FP32, B2G_LAYOUT_KN, 8, fuse, 0, 1}};
+  b2g_plan_info info;
+  size_t packed = 0, ws = 0;
+  b2g_status st = b2g_plan_for_device(&f, 148, 232448, 8, &info, &packed, &ws);
+  if (st != B2G_OK) {{ printf("error %s\\n", b2g_status_string(st)); return 1; }}
+  printf("%d %d %d %d %zu\\n", K, N, info.grid, info.partition, packed);
+  return 0;
+}}
+int main(void) {{
+  printf("version %d entries %zu\\n", (int)b2g_version(), sizeof every_entry / sizeof every_entry[0]);
+  return plan(3072, 8192, B2G_FUSE_GATE_UP_SILU | B2G_FUSE_RMSNORM_INPUT) | plan(8192, 3072, B2G_FUSE_RESIDUAL_ADD);
+}}
+""")
+    libdir = b2g.LIB_PATH.parent
+    exe = tmp_path / "consumer"
+    subprocess.run([cc, "-std=c11", "-Wall", "-Wextra", "-Werror", "-Wno-cast-function-type", "-I", str(ROOT / "include"),
+                    str(src), "-L", str(libdir), "-lb200gemv", f"-Wl,-rpath,{libdir}", "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    assert out[0].startswith("version ") and out[0].endswith(f"entries {len(declared_functions())}")
+    assert out[1] == f"3072 8192 128 2 {2 * 3072 * 8192}"
+    assert out[2] == f"8192 3072 96 2 {8192 * 3072}"
