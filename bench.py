@@ -7,8 +7,10 @@ One step = one decode step of M tokens through all 28 layers
 (RMSNorm -> fused gate||up + SiLU*up -> down + residual), weights resident in
 HBM (2.12 GB of E4M3 per step, far above the 126 MB L2, so every step streams
 from HBM without an explicit flush).  With N > 1 (torchrun), the stack is
-tensor-parallel: gate/up column shards, down K shards, and an NCCL fp16
-all-reduce of the 3072-wide partials per layer.
+tensor-parallel: gate/up column shards, down K shards, and one fp16 sum of
+the 3072-wide partials per layer -- fused into the GEMVs over peer memory
+(--tp-mode fused, the default) or an NCCL all-reduce between them
+(--tp-mode nccl).
 
 Prints one JSON line (rank 0): value = algorithmic HBM TB/s of the whole job
 (bytes all ranks stream / max-over-ranks device time), plus us/layer, the
@@ -335,13 +337,13 @@ def run_ours(args):
     M = args.m
     inter = INTER // tp
     if tp == 1:
-        # One GPU: the library's stack (one cooperative launch for all layers).
+        # One GPU: the library's stack (two launches per layer, chained).
         st = b2g.Stack(HIDDEN, INTER, LAYERS, max_m=M)
         gu_op, dn_op = st.gate_up, st.down
         tps = None
     else:
         # Tensor parallel: the package's TPStack (column/K shards, residual on
-        # rank 0, NCCL all-reduce of the partials per layer).
+        # rank 0, the partials summed per layer: fused exchange or NCCL).
         import importlib
         st = None
         tps = importlib.import_module("b2g.tp").TPStack(HIDDEN, INTER, LAYERS, rank=rank, world=world, max_m=M,
