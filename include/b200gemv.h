@@ -327,7 +327,8 @@ b2g_status b2g_stack_workspace_init(const b2g_stack* st, void* workspace, b2g_st
 /* Execution mode (key B2G_STACK_OPT_MODE):
  *  PER_LAYER (default): two launches per layer chained with programmatic
  *    dependent launch; each launch first loads its own leading weights, then
- *    asks L2 for the next launch's whole range.
+ *    asks L2 for the first 256 KB of each range the next launch's CTAs will
+ *    stream.
  *  PERSISTENT: one cooperative launch runs every layer (up to 32 layers per
  *    launch), grid barriers between the gate||up and down phases; each
  *    phase's first weights are loaded while the barrier completes.
