@@ -113,9 +113,9 @@ typedef struct {
                              after the wait). */
   const void* prefetch_packed; /* optional: packed weights of the kernel that
                                   will follow this one in the stream; at its
-                                  start each CTA asks L2 to fetch the range
-                                  that kernel's CTA of the same index will
-                                  stream (NULL = off) */
+                                  start CTA c asks L2 for the first 256 KB of
+                                  the ranges that kernel's CTAs c, c + grid,
+                                  ... will stream (NULL = off) */
   const struct b2g_op* prefetch_op; /* the op prefetch_packed belongs to */
 } b2g_enqueue_args;
 
