@@ -331,10 +331,12 @@ def load_layers(wf: WeightFile, st, device, layers=None, quantize=None, verify: 
             continue
         full = {}
         for proj in ("gate_proj", "up_proj", "down_proj"):
-            try:
-                rec = wf.find(layer, proj, KIND_FP16_KN)
-            except KeyError:
-                rec = wf.find(layer, proj, KIND_E4M3_KN)
+            src = [r for r in wf.records if r.layer == layer and r.proj == proj and r.tp_size == 1
+                   and r.kind in (KIND_FP16_KN, KIND_E4M3_KN)]
+            if not src:
+                raise WeightFileError(f"layer {layer}: no packed records for rank {rank} of {world} that fit "
+                                      f"this op, and no source weights for {proj}")
+            rec = min(src, key=lambda r: r.kind)  # fp16 source first, else E4M3 codes
             d, s = wf.read(rec, verify)
             w = torch.from_numpy(d).to(device)
             if rec.kind == KIND_FP16_KN and e4m3:

@@ -263,3 +263,33 @@ def test_packed_export_reload_and_layout_check(wfm, tmp_path):
     with pytest.raises(wfm.WeightFileError, match="another op plan"):
         wfm.load_layers(wfm.WeightFile(tmp_path / "p.b2gw"), FakeStack(64, 128, 2, ksplit=2), "cpu",
                         quantize=no_quantize)
+
+
+def test_tp_rank_packed_export_reload(wfm, tmp_path):
+    """A TPStack rank exports its own shard's streams (records named for the
+    rank); the same rank reloads them without quantising, another rank finds
+    none of its own and falls back to the source records."""
+    orc = load_oracle()
+    tpm = importlib.import_module("b2g.tp")
+    src = tmp_path / "w"
+    src.mkdir()
+    _write_blobs(src, [0], 64, 128, True, np.random.default_rng(8))
+    wfm.import_reference_blobs(src, tmp_path / "m.b2gw")
+
+    def rank_stack(rank):
+        st = tpm.TPStack(64, 128, 1, rank=rank, world=2, build_ops=False)
+        st.gate_up, st.down = FakeOp(64, 64, 2), FakeOp(64, 64, 1)
+        return st
+    r1 = rank_stack(1)
+    wfm.load_layers(wfm.WeightFile(tmp_path / "m.b2gw"), r1, "cpu", quantize=_oracle_quantize(orc))
+    recs = wfm.export_packed(tmp_path / "r1.b2gw", r1)
+    assert [r.name for r in recs] == ["L00.gate_up.tp1of2", "L00.down_proj.tp1of2"]
+
+    def no_quantize(w, mode):
+        raise AssertionError("a packed reload must not quantise")
+    again = rank_stack(1)
+    wfm.load_layers(wfm.WeightFile(tmp_path / "r1.b2gw"), again, "cpu", quantize=no_quantize)
+    for a, b in zip(r1.layers[0], again.layers[0]):
+        assert torch.equal(a, b)
+    with pytest.raises(wfm.WeightFileError, match="rank 0 of 2"):  # no records of its own, no source weights
+        wfm.load_layers(wfm.WeightFile(tmp_path / "r1.b2gw"), rank_stack(0), "cpu", quantize=no_quantize)
