@@ -438,6 +438,22 @@ def run_ours(args):
         st.set_mode("per_layer")
         detail_extra["persistent_kernel_ms_per_step"] = round(ms_pl, 5)
         detail_extra["persistent_kernel_us_per_layer"] = round(ms_pl * 1e3 / LAYERS, 3)
+        if M != 1:
+            # The same stack at M = 1 (the metric is quoted at M = 1 and 8);
+            # recorded, not fatal.
+            try:
+                h1, act1 = h[:1].clone(), act[:1].clone()
+
+                def step_m1():
+                    st.enqueue(h1, act1, ws)
+                for _ in range(3):
+                    step_m1()
+                ms1 = timed(step_m1, reps) / reps
+                b1 = sum(layer_bytes(1, tp)) * LAYERS
+                detail_extra["stack_m1_us_per_layer"] = round(ms1 * 1e3 / LAYERS, 3)
+                detail_extra["stack_m1_tb_s"] = round(b1 / (ms1 * 1e-3) / 1e12, 4)
+            except Exception as e:
+                detail_extra["stack_m1_error"] = f"{type(e).__name__}: {e}"
 
     # ---- dominant kernel: the fused RMSNorm + gate||up + SiLU*up GEMV (two
     # thirds of the bytes), its 28 layers back to back exactly as the step
