@@ -255,7 +255,11 @@ b2g_status b2g_enqueue_static(const b2g_op* op, const b2g_enqueue_args* args, b2
  * layers alternate between the inbox's two buffers (`buf`).  A wait that
  * expires sets the device error word (B2G_ERR_PEER_TIMEOUT class, code 4);
  * while the word is set, later waits give up at once (a lost peer costs one
- * 2 s wait, not one per layer) and skip their writes.
+ * 2 s wait, not one per layer).  b2g_tp_gather then leaves h as it was; a
+ * GATHER launch still runs its GEMV on whatever its inbox holds.  Either way
+ * every row produced since the error is invalid: read and clear the word
+ * (b2g_device_error), then re-zero the exchange buffers and the ops'
+ * workspaces (b2g_workspace_init) before the next step.
  * ------------------------------------------------------------------------ */
 #define B2G_TP_MAX_RANKS 8
 enum { B2G_TP_NONE = 0, B2G_TP_PUSH = 1, B2G_TP_GATHER = 2 };
