@@ -1,4 +1,4 @@
-"""Tensor-parallel stack host logic on CPU: two gloo ranks (world size 2).
+"""Tensor-parallel stack host logic on CPU: gloo ranks (world size 2 and 4).
 
 Each rank runs the package's TPStack orchestration -- shard ranges, which
 weights and scales each rank slices, the residual on rank 0 only, the
@@ -90,14 +90,15 @@ def test_shard_range(b2g):
         tp.shard_range(8192, 2, 2)
 
 
-def test_tp_stack_two_gloo_ranks(b2g, orc, syn, tmp_path):
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_stack_gloo_ranks(b2g, orc, syn, tmp_path, world):
     out = str(tmp_path / "h.npy")
     mp.spawn(_worker, args=(world, _free_port(), out), nprocs=world, join=True)
     got, h0 = np.load(out)
-    lo0, hi0 = map(int, open(out + ".shards").read().split())
-    lo1, hi1 = map(int, open(out + ".shards1").read().split())
-    assert (lo0, hi0, lo1, hi1) == (0, INTER // 2, INTER // 2, INTER)
+    shards = [tuple(map(int, open(out + (".shards" if r == 0 else f".shards{r}")).read().split()))
+              for r in range(world)]
+    step = INTER // world
+    assert shards == [(r * step, (r + 1) * step) for r in range(world)]
     layers = _layers(orc, syn)
     want_tp = h0
     for L in layers:
