@@ -469,25 +469,36 @@ b2g_status b2g_enqueue_ex(const b2g_op* op, const b2g_enqueue_args* a, b2g_strea
   return enqueue_impl(op, a, nullptr, stream);
 }
 
-static b2g_status enqueue_impl(const b2g_op* op, const b2g_enqueue_args* a, const TpParams* tp,
-                               b2g_stream_t stream) {
+// The checks of an enqueue's arguments that need no device (the workspace
+// pointer is checked unless `own_workspace`: the static entry point supplies it).
+static b2g_status check_args(const b2g_op* op, const b2g_enqueue_args* a, bool own_workspace) {
   if (!op || !a) return B2G_ERR_INVALID;
   if (a->m < 1 || a->m > op->f.max_m) return B2G_ERR_INVALID;
-  if (!a->x || !a->packed_w || !a->y || !a->workspace) return B2G_ERR_INVALID;
+  if (!a->x || !a->packed_w || !a->y || (!own_workspace && !a->workspace)) return B2G_ERR_INVALID;
   if (op->f.scale_mode != B2G_SCALE_NONE && !a->scales) return B2G_ERR_INVALID;
   const bool resid = (op->f.fuse & B2G_FUSE_RESIDUAL_ADD) != 0;
   if (resid && !a->residual) return B2G_ERR_INVALID;
   if (a->ldx < op->K || a->ldy < op->N || (resid && a->ldr < op->N)) return B2G_ERR_INVALID;
-  if (!aligned(a->packed_w, 16) || !aligned(a->workspace, 16)) return B2G_ERR_INVALID;
+  if (!aligned(a->packed_w, 16) || (!own_workspace && !aligned(a->workspace, 16))) return B2G_ERR_INVALID;
   if (!aligned(a->x, 2) || !aligned(a->y, 2)) return B2G_ERR_INVALID;
   if (op->f.scale_mode == B2G_SCALE_CHANNEL_FP32 && !aligned(a->scales, 4)) return B2G_ERR_INVALID;
+  if (a->prefetch_op && a->prefetch_packed && !aligned(a->prefetch_packed, 16)) return B2G_ERR_INVALID;
+  LaunchPlan lp;
+  if (!plan_launch(op, a->m, &lp)) return B2G_ERR_OOM;
+  return B2G_OK;
+}
+
+static b2g_status enqueue_impl(const b2g_op* op, const b2g_enqueue_args* a, const TpParams* tp,
+                               b2g_stream_t stream) {
+  b2g_status st = check_args(op, a, false);
+  if (st != B2G_OK) return st;
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess) return B2G_ERR_CUDA;
   if (dev != op->device) return B2G_ERR_INVALID;
-  b2g_status st = ensure_device_setup(dev, op->smem_optin);
+  st = ensure_device_setup(dev, op->smem_optin);
   if (st != B2G_OK) return st;
   LaunchPlan lp;
-  if (!plan_launch(op, a->m, &lp)) return B2G_ERR_OOM;
+  plan_launch(op, a->m, &lp);
 
   GemvParams p = {};
   fill_plan(op, a->m, lp, a->workspace, dev, &p);
@@ -502,7 +513,6 @@ static b2g_status enqueue_impl(const b2g_op* op, const b2g_enqueue_args* a, cons
   p.rms_eps = a->rms_eps;
   if (a->prefetch_op && a->prefetch_packed) {
     const b2g_op* nx = a->prefetch_op;
-    if (!aligned(a->prefetch_packed, 16)) return B2G_ERR_INVALID;
     p.pf_packed = static_cast<const uint8_t*>(a->prefetch_packed);
     p.pf_total_units = nx->total_units;
     p.pf_gran = nx->gran;
@@ -565,9 +575,15 @@ b2g_status b2g_enqueue_static(const b2g_op* op, const b2g_enqueue_args* args, b2
   b2g_status st = b2g_workspace_size(op, args->m, &need);
   if (st != B2G_OK) return st;
   if (need > B2G_STATIC_SCRATCH_BYTES) return B2G_ERR_SCRATCH_LIMIT;
+  // Every argument is checked before anything is queued: a refused call
+  // leaves the stream untouched.
+  st = check_args(op, args, true);
+  if (st != B2G_OK) return st;
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess) return B2G_ERR_CUDA;
   if (dev != op->device || dev < 0 || dev >= 64) return B2G_ERR_INVALID;
+  st = ensure_device_setup(dev, op->smem_optin);
+  if (st != B2G_OK) return st;
   void* ws = nullptr;
   {
     std::lock_guard<std::mutex> lk(g_mu);

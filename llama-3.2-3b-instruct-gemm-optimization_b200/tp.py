@@ -51,6 +51,10 @@ class TPStack:
         self.layers = [None] * n_layers
         self.gate_up = self.down = None
         self.fused = fused
+        # Exchange rounds pushed so far (one per layer, carried across calls):
+        # round r uses inbox buffer r % 2, so consecutive pushes always
+        # alternate, also from the last layer of one call to the first of the next.
+        self._round = 0
         self.comm = None
         self._comm_buf = None
         self._peer_bases = []
@@ -168,6 +172,12 @@ class TPStack:
         if self.comm is None:
             raise RuntimeError("fused TPStack needs setup_comm() first")
         n = self.n_layers
+        import torch
+        if n % 2 and torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+            # A graph fixes each launch's buffer; with an odd layer count the
+            # replays would not alternate (the last push of one replay and the
+            # first of the next would share a buffer a peer may still read).
+            raise ValueError(f"a CUDA graph of the fused exchange needs an even layer count, not {n}")
         for layer in range(n):
             pgu, sgu, pd, sd = self.layers[layer]
             if layer == 0:
@@ -175,12 +185,13 @@ class TPStack:
                                      prefetch=(self.down, pd))
             else:
                 # h = sum of the ranks' previous down outputs, summed here
-                self.gate_up.enqueue_tp(self.comm, TP_GATHER, (layer - 1) % 2, h, pgu, sgu, y=act,
+                self.gate_up.enqueue_tp(self.comm, TP_GATHER, (self._round - 1) % 2, h, pgu, sgu, y=act,
                                         workspace=workspace, rms_eps=self.rms_eps, pdl=True,
                                         prefetch=(self.down, pd), push_op=self.down, h_out=h)
             nxt = self.layers[(layer + 1) % n]
-            self.down.enqueue_tp(self.comm, TP_PUSH, layer % 2, act, pd, sd, y=h, workspace=workspace,
+            self.down.enqueue_tp(self.comm, TP_PUSH, self._round % 2, act, pd, sd, y=h, workspace=workspace,
                                  residual=h if self.rank == 0 else None, pdl=True,
                                  prefetch=None if nxt is None else (self.gate_up, nxt[0]))
-        tp_gather(self.comm, (n - 1) % 2, self.down, h)
+            self._round += 1
+        tp_gather(self.comm, (self._round - 1) % 2, self.down, h)
         return h

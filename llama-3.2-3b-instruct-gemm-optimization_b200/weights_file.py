@@ -330,6 +330,7 @@ def load_layers(wf: WeightFile, st, device, layers=None, quantize=None, verify: 
             st.set_layer(layer, *tens)
             continue
         full = {}
+        hidden, inter = gu_op.K, gu_op.N * world  # whole matrices (a TP op holds one shard of I)
         for proj in ("gate_proj", "up_proj", "down_proj"):
             src = [r for r in wf.records if r.layer == layer and r.proj == proj and r.tp_size == 1
                    and r.kind in (KIND_FP16_KN, KIND_E4M3_KN)]
@@ -337,7 +338,13 @@ def load_layers(wf: WeightFile, st, device, layers=None, quantize=None, verify: 
                 raise WeightFileError(f"layer {layer}: no packed records for rank {rank} of {world} that fit "
                                       f"this op, and no source weights for {proj}")
             rec = min(src, key=lambda r: r.kind)  # fp16 source first, else E4M3 codes
+            want_kn = (inter, hidden) if proj == "down_proj" else (hidden, inter)
+            if (rec.K, rec.N) != want_kn:
+                raise WeightFileError(f"{rec.name}: {rec.K}x{rec.N} weights, the stack needs "
+                                      f"{want_kn[0]}x{want_kn[1]}")
             d, s = wf.read(rec, verify)
+            if rec.kind == KIND_E4M3_KN:
+                _check_code_scales(rec, s, gu_op.scale_mode)
             w = torch.from_numpy(d).to(device)
             if rec.kind == KIND_FP16_KN and e4m3:
                 full[proj] = quantize(w, gu_op.scale_mode)
@@ -351,6 +358,20 @@ def load_layers(wf: WeightFile, st, device, layers=None, quantize=None, verify: 
         else:
             sgu = None if sg is None else torch.cat([sg, su]).contiguous()
             st.set_layer(layer, gu_op.prepack(qg, qu), sgu, dn_op.prepack(qd), sd)
+
+
+def _check_code_scales(rec: Record, s, scale_mode: int) -> None:
+    """E4M3 codes are used as they are, so their scale rule must be the op's
+    and their scales exactly what the kernel reads for it: none, one fp16
+    (tensor), N fp16 or N fp32 (per channel)."""
+    if rec.scale_mode != scale_mode:
+        raise WeightFileError(f"{rec.name}: codes quantised with scale mode {rec.scale_mode}, "
+                              f"the op uses {scale_mode}")
+    want = {0: (0, None), 1: (1, np.float16), 2: (rec.N, np.float16), 3: (rec.N, np.float32)}[scale_mode]
+    have = (0, None) if s is None else (s.size, s.dtype.type)
+    if have != want:
+        raise WeightFileError(f"{rec.name}: {have[0]} scales of {have[1]}, scale mode {scale_mode} "
+                              f"needs {want[0]} of {want[1]}")
 
 
 def packed_layout(op) -> tuple:

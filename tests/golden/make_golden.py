@@ -1,9 +1,10 @@
 """Generate the golden fixtures in tests/golden/ from the reference's own code.
 
-Run in a container that has the reference checkout (default /root/reference)
-after ``make -C oracle`` has built oracle/_ref/ from the reference sources:
+Run in a container that has the reference checkout, after
+``make -C oracle REF=<checkout>`` has built oracle/_ref/ from the reference
+sources:
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <checkout>
 
 Fixtures written (all small, committed):
 
@@ -145,7 +146,7 @@ def cfg0():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="the reference checkout")
     a = ap.parse_args()
     if orc.ref() is None or not orc.KAT_TOOL.exists():
         sys.exit("oracle/_ref is not built: run `make -C oracle` with the reference present")

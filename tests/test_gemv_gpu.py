@@ -246,20 +246,48 @@ def test_ksplit_ranges(b2g, orc, syn, cuda, ks, part, grid):
 
 
 def test_refused_option_keeps_plan(b2g, orc, syn, cuda):
-    """8 K ranges on 148 CTAs would need more than 8 tiles per CTA: refused,
-    and the op keeps its previous, working plan."""
+    """A grid of one CTA would hand it all 192 tiles of 8192->3072, far more
+    than its 8 shared slots: no valid plan, so the option is refused and the
+    op keeps its previous, working plan.  A K split that does not divide the
+    256 k-blocks (3) is refused as invalid."""
     K, N = 8192, 3072
     op = b2g.GemvOp(K, N, weight_dtype=1, scale_mode=3, max_m=8)
     before = op.plan(8)
     with pytest.raises(b2g.B2GError) as e:
-        op.set_option(b2g.OPT_KSPLIT, 8)
+        op.set_option(b2g.OPT_GRID, 1)
     assert e.value.status == b2g.ERR_UNSUPPORTED
+    assert op.plan(8) == before
+    with pytest.raises(b2g.B2GError) as e:
+        op.set_option(b2g.OPT_KSPLIT, 3)
+    assert e.value.status == b2g.ERR_INVALID
     assert op.plan(8) == before
     Wd, Wh, s = make_weights(orc, syn, 38, K, N, 1, 3)
     x = syn.activations(60, 8, K)
     y = op.enqueue(dev(x), op.prepack(Wd), dev(s))
     torch.cuda.synchronize()
     check(orc, y, orc.gemv(Wh, orc.WTYPE_FP8, x, 3, s), 1)
+
+
+def test_ksplit_8_plans_in_waves(b2g, orc, syn, cuda):
+    """K split into 8 ranges of 8192->3072 gives 1536 virtual tiles: one CTA
+    per SM would touch more than its 8 slots, so the planner grows the grid
+    into waves of CTAs with at most 7 whole tiles each; the result still
+    matches the oracle."""
+    K, N = 8192, 3072
+    op = b2g.GemvOp(K, N, weight_dtype=1, scale_mode=3, max_m=8)
+    op.set_option(b2g.OPT_KSPLIT, 8)
+    plan = op.plan(8)
+    assert plan["ksplit"] == 8
+    assert plan["grid"] > torch.cuda.get_device_properties(0).multi_processor_count
+    assert plan["n_slots"] <= 8
+    Wd, Wh, s = make_weights(orc, syn, 39, K, N, 1, 3)
+    packed = op.prepack(Wd)
+    for M in (1, 8):
+        x = syn.activations(61 + M, M, K)
+        y = op.enqueue(dev(x), packed, dev(s))
+        torch.cuda.synchronize()
+        check(orc, y, orc.gemv(Wh, orc.WTYPE_FP8, x, 3, s), 1, ("ksplit8", M))
+    assert b2g.device_error() == 0
 
 
 def test_deterministic_and_rows_independent(b2g, orc, syn, cuda):

@@ -112,9 +112,9 @@ def test_tp_stack_gloo_ranks(b2g, orc, syn, tmp_path, world):
 def test_fused_exchange_schedule(b2g, monkeypatch):
     """TPStack(fused=True)'s launch order on one rank, with recording stand-ins
     for the ops: layer 0 stages h plainly; every later gate||up gathers the
-    previous layer's pushes from buffer (l - 1) % 2 (and writes h); every down
-    pushes into buffer l % 2, with the residual on rank 0 only; one final
-    gather reads buffer (n - 1) % 2.  Each launch prefetches the next one's
+    previous push from its buffer (and writes h); push number r (counted over
+    all calls) goes to buffer r % 2, with the residual on rank 0 only; one
+    final gather reads the last push's buffer.  Each launch prefetches the next one's
     weights."""
     tp_mod = __import__("b2g.tp", fromlist=["TPStack"])
     calls = []
@@ -151,3 +151,12 @@ def test_fused_exchange_schedule(b2g, monkeypatch):
                          ("gu", G, 0, "pgu1", "pd1"), ("dn", Pu, 1, "pd1", "pgu2"),
                          ("gu", G, 1, "pgu2", "pd2"), ("dn", Pu, 0, "pd2", "pgu0"),
                          ("final", "gather", 0, None, None)], rank
+        # A second call continues the alternation: with 3 layers the first
+        # push of this call goes to buffer 1, not to buffer 0, which a peer's
+        # final gather of the previous call may still be reading.
+        calls.clear()
+        st.enqueue(h, act, None)
+        assert calls == [("gu", "plain", None, "pgu0", "pd0"), ("dn", Pu, 1, "pd0", "pgu1"),
+                         ("gu", G, 1, "pgu1", "pd1"), ("dn", Pu, 0, "pd1", "pgu2"),
+                         ("gu", G, 0, "pgu2", "pd2"), ("dn", Pu, 1, "pd2", "pgu0"),
+                         ("final", "gather", 1, None, None)], rank

@@ -293,3 +293,48 @@ def test_tp_rank_packed_export_reload(wfm, tmp_path):
         assert torch.equal(a, b)
     with pytest.raises(wfm.WeightFileError, match="rank 0 of 2"):  # no records of its own, no source weights
         wfm.load_layers(wfm.WeightFile(tmp_path / "r1.b2gw"), rank_stack(0), "cpu", quantize=no_quantize)
+
+
+def _e4m3_items(wfm, rng, hidden, inter, mode, n_scales=None, shape=None):
+    """One layer of E4M3_KN records with scale mode `mode` (codes random)."""
+    R = wfm.Record
+    items = []
+    for proj, (K, N) in (("gate_proj", (hidden, inter)), ("up_proj", (hidden, inter)),
+                         ("down_proj", (inter, hidden))):
+        if shape is not None and proj == "down_proj":
+            K, N = shape
+        codes = rng.integers(0, 0x7F, (K, N), dtype=np.uint8)
+        n = N if n_scales is None else n_scales
+        s = None if mode == 0 else (rng.random(n).astype(np.float32 if mode == 3 else np.float16))
+        items.append((R(0, proj, wfm.KIND_E4M3_KN, 1, mode, K, N), codes, s))
+    return items
+
+
+def test_e4m3_source_records_checked_against_op(wfm, tmp_path):
+    """E4M3 codes are used without re-quantising, so a record whose scale
+    rule, scale count or shape is not the op's is refused: the kernel would
+    otherwise read N per-channel scales from a one-value buffer."""
+    rng = np.random.default_rng(9)
+
+    def no_quantize(w, mode):
+        raise AssertionError("E4M3 records are not re-quantised")
+    # matching records load (per-channel FP32, the op's rule)
+    wfm.write(tmp_path / "ok.b2gw", _e4m3_items(wfm, rng, 64, 128, 3))
+    st = FakeStack(64, 128, 1)
+    wfm.load_layers(wfm.WeightFile(tmp_path / "ok.b2gw"), st, "cpu", quantize=no_quantize)
+    assert st._keep[0][3].numel() == 64
+    # per-tensor codes into a per-channel op
+    wfm.write(tmp_path / "tensor.b2gw", _e4m3_items(wfm, rng, 64, 128, 1, n_scales=1))
+    with pytest.raises(wfm.WeightFileError, match="scale mode 1"):
+        wfm.load_layers(wfm.WeightFile(tmp_path / "tensor.b2gw"), FakeStack(64, 128, 1), "cpu",
+                        quantize=no_quantize)
+    # right rule, wrong number of scales
+    wfm.write(tmp_path / "count.b2gw", _e4m3_items(wfm, rng, 64, 128, 3, n_scales=5))
+    with pytest.raises(wfm.WeightFileError, match="5 scales"):
+        wfm.load_layers(wfm.WeightFile(tmp_path / "count.b2gw"), FakeStack(64, 128, 1), "cpu",
+                        quantize=no_quantize)
+    # a down projection of another shape
+    wfm.write(tmp_path / "shape.b2gw", _e4m3_items(wfm, rng, 64, 128, 3, shape=(96, 64)))
+    with pytest.raises(wfm.WeightFileError, match="96x64"):
+        wfm.load_layers(wfm.WeightFile(tmp_path / "shape.b2gw"), FakeStack(64, 128, 1), "cpu",
+                        quantize=no_quantize)
