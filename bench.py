@@ -191,13 +191,98 @@ def adjacent_shapes(b2g, torch, device, M: int, reps: int = 5) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# Per-configuration figures: each GEMV of the decode MLP on its own, chained
+# over 28 distinct weight sets (2.1 GB for FP8 U + D, 1.4 GB for FP16 U:
+# every launch streams from HBM), with programmatic dependent launch and the
+# L2 prefetch of the next launch's weights exactly as the stack chains them.
+# ---------------------------------------------------------------------------
+def _chain_us(torch, launches, reps: int) -> float:
+    """Device time per launch of a chain of launches (CUDA events on the
+    launching stream, after 3 warm-up passes)."""
+    for _ in range(3):
+        for f in launches:
+            f()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        for f in launches:
+            f()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / (reps * len(launches))
+
+
+def gemv_bytes(K: int, N: int, M: int, wbytes: int, scale_bytes: int) -> int:
+    """Algorithmic bytes of one GEMV: W + scales + x + y."""
+    return K * N * wbytes + N * scale_bytes + 2 * M * K + 2 * M * N
+
+
+def per_config(b2g, torch, device, layers, hbm: float, ms: tuple, reps: int = 5) -> dict:
+    """FP16 U at M=1; FP8 U (3072->8192) and D (8192->3072) at M in ms; the
+    CUDA-core FFMA variant against the tensor-core path at M=8.  Needs every
+    layer's raw E4M3 codes (layers[l]["q0"])."""
+    out = {}
+
+    def rec(name, K, N, M, us, alg, **kw):
+        out[name] = {"K": K, "N": N, "m": M, "us_per_launch": round(us, 3), "alg_bytes": alg,
+                     "achieved_gbs": round(alg / us / 1e3, 1), "frac_of_measured_hbm": round(alg / us / 1e3 / hbm, 4),
+                     **kw}
+
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
+    xs = {M: torch.randn(M, INTER, generator=g, device=device, dtype=torch.float32).half() for M in ms}
+    y = torch.empty(max(ms), INTER, dtype=torch.float16, device=device)
+    for name, (K, N, j) in {"fp8_U": (HIDDEN, INTER, 0), "fp8_D": (INTER, HIDDEN, 2)}.items():
+        op = b2g.GemvOp(K, N, max_m=8)
+        packs = [op.prepack(layers[l]["q0"][j]) for l in range(LAYERS)]
+        scales = [layers[l]["sd"] if j == 2 else layers[l]["sgu"][:INTER] for l in range(LAYERS)]
+        ws = op.workspace(device)
+        for M in ms:
+            x = xs[M][:, :K]
+            x = x.contiguous()
+
+            def mk(i, op=op, x=x, M=M):
+                return lambda: op.enqueue(x, packs[i], scales[i], y=y[:M, :N], workspace=ws, pdl=True,
+                                          prefetch=(op, packs[(i + 1) % LAYERS]))
+            us = _chain_us(torch, [mk(i) for i in range(LAYERS)], reps)
+            rec(f"{name}_m{M}", K, N, M, us, gemv_bytes(K, N, M, 1, 4), grid=op.plan(M)["grid"])
+        if 8 in ms:
+            # north-star item: CUDA-core FFMA against mma.sync at M = 8
+            op.set_option(b2g.OPT_MATH, b2g.MATH_FFMA)
+            x = xs[8][:, :K].contiguous()
+            us = _chain_us(torch, [(lambda i=i: op.enqueue(x, packs[i], scales[i], y=y[:8, :N], workspace=ws, pdl=True,
+                                                           prefetch=(op, packs[(i + 1) % LAYERS])))
+                                   for i in range(LAYERS)], reps)
+            rec(f"{name}_m8_ffma", K, N, 8, us, gemv_bytes(K, N, 8, 1, 4), grid=op.plan(8)["grid"])
+        del packs
+    # FP16 U, M = 1: W ~ N(0, 0.02) and x ~ N(0, 1), 28 distinct weight sets
+    op = b2g.GemvOp(HIDDEN, INTER, weight_dtype="fp16", scale_mode="none", max_m=8)
+    raw, packs = [], []
+    for l in range(LAYERS):
+        gl = torch.Generator(device=device)
+        gl.manual_seed(l)
+        w = (torch.randn(HIDDEN, INTER, generator=gl, device=device, dtype=torch.float32) * 0.02).half()
+        packs.append(op.prepack(w))
+        raw.append(w)
+    x = torch.randn(1, HIDDEN, generator=g, device=device, dtype=torch.float32).half()
+    ws = op.workspace(device)
+    us = _chain_us(torch, [(lambda i=i: op.enqueue(x, packs[i], None, y=y[:1], workspace=ws, pdl=True,
+                                                   prefetch=(op, packs[(i + 1) % LAYERS])))
+                           for i in range(LAYERS)], reps)
+    rec("fp16_U_m1", HIDDEN, INTER, 1, us, gemv_bytes(HIDDEN, INTER, 1, 2, 0), grid=op.plan(1)["grid"])
+    del packs
+    return out, raw
+
+
+# ---------------------------------------------------------------------------
 # The reference's own GPU kernels (kernels/gemv_fp8.cu run_gemv, compiled for
 # sm_100a by baseline/Makefile) on the same weights
 # ---------------------------------------------------------------------------
 REF_GPU_LIB = ROOT / "baseline" / "_ref" / "libref_gpu.so"
 
 
-def reference_kernels(torch, layers, h, M: int, our_ms_per_step: float):
+def reference_kernels(torch, layers, h, M: int, our_ms_per_step: float, fp16_sets=None):
     """Times the reference GEMV path on the 28-layer stack: per layer and token
     its three M=1 GEMVs (gate, up, down; memset + gemv_chunk_kernel + cast
     each, kernels/gemv_fp8.cu:276-283), M tokens one after another (the
@@ -231,6 +316,7 @@ def reference_kernels(torch, layers, h, M: int, our_ms_per_step: float):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / reps
 
+    L.ref_gpu_gemv_fp16.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4
     shapes = {"gate_up": (HIDDEN, INTER, 0, x), "down": (INTER, HIDDEN, 2, a)}
     best, shipped = {}, {}
     for name, (K, N, j, xv) in shapes.items():
@@ -249,6 +335,23 @@ def reference_kernels(torch, layers, h, M: int, our_ms_per_step: float):
         us, cfg = min(results)
         best[name] = {"cfg": cfg, "us": round(us, 2)}
 
+    # The reference's FP16 GEMV (kernels/gemv_fp16.cu run_gemv) at 3072 -> 8192,
+    # M = 1, over 28 distinct FP16 weight sets: best of its variant x grid sweep.
+    fp16_best = None
+    if fp16_sets is not None:
+        def gemv16(w, cfg):
+            st = L.ref_gpu_gemv_fp16(w.data_ptr(), x.data_ptr(), y_acc.data_ptr(), y.data_ptr(), HIDDEN, INTER, *cfg)
+            if st != 0:
+                raise RuntimeError(f"reference fp16 gemv failed: CUDA error {st}")
+        res16 = []
+        for variant in range(4):
+            for grid in (14, 29, 48, 96, 148, 296, 592):
+                cfg = (variant, grid)
+                timed(lambda: [gemv16(w, cfg) for w in fp16_sets], 1)
+                res16.append((timed(lambda: [gemv16(w, cfg) for w in fp16_sets], 2) * 1e3 / len(fp16_sets), cfg))
+        us16, cfg16 = min(res16)
+        fp16_best = {"us": round(us16, 2), "cfg_variant_grid": cfg16}
+
     def step():
         for l in range(LAYERS):
             qg, qu, qd = layers[l]["q0"]
@@ -264,6 +367,7 @@ def reference_kernels(torch, layers, h, M: int, our_ms_per_step: float):
             "per_gemv_us_best": {k: v["us"] for k, v in best.items()},
             "best_cfg_variant_grid_ku": {k: v["cfg"] for k, v in best.items()},
             "per_gemv_us_shipped_l4_cfg": {k: v["us"] for k, v in shipped.items()},
+            "fp16_gate_up_m1_best": fp16_best,
             "ours_speedup": round(ms / our_ms_per_step, 2)}
 
 
@@ -438,22 +542,31 @@ def run_ours(args):
         st.set_mode("per_layer")
         detail_extra["persistent_kernel_ms_per_step"] = round(ms_pl, 5)
         detail_extra["persistent_kernel_us_per_layer"] = round(ms_pl * 1e3 / LAYERS, 3)
-        if M != 1:
-            # The same stack at M = 1 (the metric is quoted at M = 1 and 8);
-            # recorded, not fatal.
+        # The same stack at every M of the metric's configs (one decode MLP
+        # layer = fused gate||up + down, 28 distinct layers per step), each
+        # replayed as a CUDA graph of one step; recorded, not fatal.
+        per_m = {}
+        for Mi in (1, 2, 4, 8):
             try:
-                h1, act1 = h[:1].clone(), act[:1].clone()
+                hi, acti = h0[:Mi].clone(), act[:Mi].clone()
 
-                def step_m1():
-                    st.enqueue(h1, act1, ws)
+                def step_mi():
+                    st.enqueue(hi, acti, ws)
+                step_mi()
+                gi = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gi):
+                    step_mi()
                 for _ in range(3):
-                    step_m1()
-                ms1 = timed(step_m1, reps) / reps
-                b1 = sum(layer_bytes(1, tp)) * LAYERS
-                detail_extra["stack_m1_us_per_layer"] = round(ms1 * 1e3 / LAYERS, 3)
-                detail_extra["stack_m1_tb_s"] = round(b1 / (ms1 * 1e-3) / 1e12, 4)
+                    gi.replay()
+                msi = timed(gi.replay, reps) / reps
+                gi.reset()
+                bi = sum(layer_bytes(Mi, tp)) * LAYERS
+                per_m[f"m{Mi}"] = {"us_per_layer": round(msi * 1e3 / LAYERS, 3),
+                                   "tb_s": round(bi / (msi * 1e-3) / 1e12, 4),
+                                   "frac_of_measured_hbm": round(bi / (msi * 1e-3) / 1e9 / peaks()[0], 4)}
             except Exception as e:
-                detail_extra["stack_m1_error"] = f"{type(e).__name__}: {e}"
+                per_m[f"m{Mi}"] = {"error": f"{type(e).__name__}: {e}"}
+        detail_extra["stack_per_m"] = per_m
 
     # ---- dominant kernel: the fused RMSNorm + gate||up + SiLU*up GEMV (two
     # thirds of the bytes), its 28 layers back to back exactly as the step
@@ -499,10 +612,31 @@ def run_ours(args):
     ms_e2e = timed(e2e_step, k_e2e) / k_e2e
     e2e_value = bytes_rank * tp / (ms_e2e * 1e-3) / 1e12
 
+    # ---- every GEMV configuration on its own (one GPU; recorded, not fatal)
+    cfgs, fp16_raw = None, None
+    if tp == 1 and want_ref:
+        try:
+            cfgs, fp16_raw = per_config(b2g, torch, device, layers, hbm, (1, 2, 4, 8))
+        except Exception as e:
+            cfgs = {"error": f"{type(e).__name__}: {e}"}
+
     # ---- the reference's own GPU kernels on the same weights (one GPU)
     ref_k = None
     if tp == 1 and not args.no_ref_kernels:
-        ref_k = reference_kernels(torch, layers, h0, M, ms_step)
+        ref_k = reference_kernels(torch, layers, h0, M, ms_step, fp16_sets=fp16_raw)
+        if isinstance(cfgs, dict) and "error" not in cfgs and "unavailable" not in ref_k:
+            # The reference has no M > 1 path: M tokens are M launches of its best config.
+            pg = ref_k["per_gemv_us_best"]
+            for name, c in cfgs.items():
+                if name.startswith("fp8_U_m") and not name.endswith("ffma"):
+                    c["reference_us"] = round(c["m"] * pg["gate_up"], 2)
+                elif name.startswith("fp8_D_m") and not name.endswith("ffma"):
+                    c["reference_us"] = round(c["m"] * pg["down"], 2)
+                elif name == "fp16_U_m1" and ref_k.get("fp16_gate_up_m1_best"):
+                    c["reference_us"] = ref_k["fp16_gate_up_m1_best"]["us"]
+                if "reference_us" in c:
+                    c["speedup_vs_reference"] = round(c["reference_us"] / c["us_per_launch"], 2)
+    del fp16_raw
 
     # ---- the model's other decode projections (one GPU; recorded, not fatal:
     # the step's numbers above stand whatever happens here)
@@ -557,6 +691,7 @@ def run_ours(args):
             "detail": {
                 **detail_extra,
                 "reference_kernels_sm100": ref_k,
+                "per_config": cfgs,
                 "adjacent_decode_projections": adj,
                 "direct_launch_ms_per_step": round(ms_direct / args.steps, 5),
                 "gate_up_us_per_launch": round(ms_gu * 1e3, 3),
@@ -590,37 +725,85 @@ def run_ours(args):
 
 
 def run_reference(args):
+    """The reference's CPU implementation of the path (its fp64 host loop,
+    kernels/gemv_fp8.cu:313-323, compiled from its sources; the oracle's C
+    port when oracle/_ref was not built) on all host cores.  One step = the
+    three E4M3 GEMVs (gate, up, down) of `n` decode layers at M tokens, n
+    chosen so that warm-up and timed steps together take about
+    --ref-seconds; the layers cycle over two distinct weight sets (150 MB,
+    beyond the host's caches).  RMSNorm, SiLU*up and the residual are not
+    part of it: the reference has no CPU code for them."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     orc = load_module("oracle", ROOT / "oracle" / "oracle.py")
-    # E4M3 weights of layer 0 with the FP32 per-channel rule, generated on the host
     syn = load_module("b2g_synthetic", PKG_DIR / "synthetic.py")
-    qs = []
-    for j, (K, N) in enumerate(((HIDDEN, INTER), (HIDDEN, INTER), (INTER, HIDDEN))):
-        q, _ = orc.quantize_e4m3(syn.weights(1000 + j, K, N), orc.SCALE_CHANNEL_FP32)
-        qs.append(q)
-    for _ in range(args.warmup and 1):
-        pass
-    per = []
-    for _ in range(max(1, args.steps)):
-        per.append(cpu_reference_sample(qs, args.m, min_seconds=args.cpu_seconds / max(1, args.steps)))
-    v = statistics.median(p["value"] for p in per)
-    cb = dict(per[0])
-    cb["value"] = v
-    us_layer = statistics.median(p["us_per_layer"] for p in per)
+    M = args.m
+    cores = orc.cpu_count()
+    R = orc.ref()
+    shapes = [(HIDDEN, INTER), (HIDDEN, INTER), (INTER, HIDDEN)]
+    sets = []
+    for l in range(2):
+        qs = []
+        for j, (K, N) in enumerate(shapes):
+            q, _ = orc.quantize_e4m3(syn.weights(1000 + 3 * l + j, K, N), orc.SCALE_CHANNEL_FP32)
+            qs.append(q)
+        sets.append(qs)
+    rng = np.random.default_rng(5)
+    xs = [rng.standard_normal((M, K), dtype=np.float32).astype(np.float16) for K, _ in shapes]
+    if R is not None:
+        kind = "reference"
+        plans = [[R.ref_cpu_plan_create(q.ctypes.data, 1, K, N, cores) for q, (K, N) in zip(qs, shapes)]
+                 for qs in sets]
+
+        def layer(i):
+            for pl, x, (K, N) in zip(plans[i % 2], xs, shapes):
+                R.ref_cpu_plan_run(pl, np.ascontiguousarray(x.view(np.uint16)), M, np.empty((M, N), np.float64))
+    else:
+        kind = "port"
+        os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+
+        def layer(i):
+            for q, x in zip(sets[i % 2], xs):
+                orc.gemv_loop(q, orc.WTYPE_FP8, x)
+    t0 = time.perf_counter()
+    layer(0)
+    t_layer = time.perf_counter() - t0
+    n = int(max(1, min(LAYERS, args.ref_seconds / (max(1, args.steps + args.warmup) * t_layer))))
+
+    def step():
+        for i in range(n):
+            layer(i)
+    for _ in range(args.warmup):
+        step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    if R is not None:
+        for pls in plans:
+            for pl in pls:
+                R.ref_cpu_plan_destroy(pl)
+    ms_step = sum(times) / len(times) * 1e3
+    nbytes = n * sum(K * N + N * 4 + 2 * M * K + 2 * M * N for K, N in shapes)
+    v = nbytes / (ms_step * 1e-3) / 1e12
+    sample = (f"each step: {n} decode layer(s) x 3 E4M3 GEMVs (3072x8192, 3072x8192, 8192x3072) at M={M} "
+              f"through the reference's fp64 host loop, K split over {cores} threads")
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "TB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": us_layer * LAYERS / 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
         "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
         "dtype": "fp8_e4m3", "data": "synthetic",
-        "config": {"workload": (f"{LAYERS}-layer Llama-3.2-3B decode MLP stack, M={args.m} (CPU sample: "
-                                f"layer 0's three E4M3 GEMVs, scaled to the stack)"),
-                   "hidden": HIDDEN, "intermediate": INTER, "layers": LAYERS, "m": args.m,
-                   "parallelism": "host cores"},
-        "us_per_layer": us_layer,
-        "cpu_baseline": cb,
+        "config": {"workload": (f"{LAYERS}-layer Llama-3.2-3B decode MLP stack, M={M}: the reference's CPU "
+                                f"loop over {n} of its layers per step (the GEMVs only: RMSNorm, SiLU*up and "
+                                f"the residual have no CPU code in the reference)"),
+                   "hidden": HIDDEN, "intermediate": INTER, "layers": LAYERS, "m": M,
+                   "layers_per_step": n, "parallelism": "host cores"},
+        "us_per_layer": round(ms_step * 1e3 / n, 1),
+        "cpu_baseline": {"value": v, "unit": "TB/s", "cores": cores, "kind": kind, "sample": sample,
+                         "seconds_timed": round(sum(times), 3)},
         "e2e": {"value": v, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -634,6 +817,8 @@ def main():
     ap.add_argument("--m", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--ref-seconds", type=float, default=60.0,
+                    help="--impl reference: host time budget of warm-up + timed steps")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ref-kernels", action="store_true", help="skip timing the reference's GPU kernels")
     ap.add_argument("--no-adjacent", action="store_true", help="skip timing qkv_proj / o_proj / lm_head")

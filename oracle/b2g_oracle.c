@@ -9,6 +9,7 @@
  * (sudb97/Llama-3.2-3B-Instruct-gemm-optimization, files cited per function):
  *
  *   - fill_host()            kernels/gemv_fp8.cu:285-295 (srand(1234), Uniform[-0.25,0.25])
+ *   - fill_x()               kernels/gemv_fp8.cu:408-413 (checkreal's x: srand(seed), same draw)
  *   - pack_e4m3()            kernels/gemv_fp8.cu:297-304 (RNE, SATFINITE, no scale)
  *   - e4m3_to_double()       kernels/gemv_fp8.cu:306-310
  *   - cpu_reference_e4m3()   kernels/gemv_fp8.cu:313-323 (fp64, k-outer, skip x==0)
@@ -145,6 +146,12 @@ void orc_fill_host_ref(uint16_t* W, size_t w_elems, uint16_t* x, int K) {
   srand(1234);
   for (size_t i = 0; i < w_elems; ++i)
     W[i] = orc_f32_to_f16(((rand() % 2001) - 1000) / 4000.0f);
+  for (int i = 0; i < K; ++i)
+    x[i] = orc_f32_to_f16(((rand() % 2001) - 1000) / 4000.0f);
+}
+
+void orc_fill_x_ref(uint16_t* x, int K, unsigned seed) {
+  srand(seed);
   for (int i = 0; i < K; ++i)
     x[i] = orc_f32_to_f16(((rand() % 2001) - 1000) / 4000.0f);
 }

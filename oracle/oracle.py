@@ -58,6 +58,7 @@ def lib():
     L.orc_e4m3_to_f64_array.argtypes = [_u8p, _sz, _f64p]
     L.orc_f64_to_f16_array.argtypes = [_f64p, _sz, _u16p]
     L.orc_fill_host_ref.argtypes = [_u16p, _sz, _u16p, ctypes.c_int]
+    L.orc_fill_x_ref.argtypes = [_u16p, ctypes.c_int, ctypes.c_uint]
     L.orc_quantize_e4m3.argtypes = [_u16p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                     ctypes.c_int, _u8p, ctypes.c_void_p]
     L.orc_quantize_e4m3.restype = ctypes.c_int
@@ -80,6 +81,7 @@ def ref():
     R = ctypes.CDLL(str(REF_LIB_PATH))
     R.ref_fill_host.argtypes = [_u16p, _sz, _u16p, ctypes.c_int, ctypes.c_int]
     R.ref_pack_e4m3.argtypes = [_u16p, _sz, _u8p]
+    R.ref_fill_x.argtypes = [_u16p, ctypes.c_int, ctypes.c_uint]
     R.ref_e4m3_to_double.argtypes = [ctypes.c_uint8]
     R.ref_e4m3_to_double.restype = ctypes.c_double
     R.ref_cpu_reference_e4m3.argtypes = [_u8p, _u16p, _f64p, ctypes.c_int, ctypes.c_int]
@@ -142,6 +144,14 @@ def fill_host_ref(K: int, N: int):
     x = np.empty(K, np.uint16)
     lib().orc_fill_host_ref(W, W.size, x, K)
     return W.view(np.float16).reshape(K, N), x.view(np.float16)
+
+
+def fill_x_ref(K: int, seed: int) -> np.ndarray:
+    """checkreal's synthetic activations (kernels/gemv_fp8.cu:408-413): srand(seed),
+    then x[i] = fp16(((rand() % 2001) - 1000) / 4000), i.e. Uniform[-0.25, 0.25]."""
+    x = np.empty(K, np.uint16)
+    lib().orc_fill_x_ref(x, K, seed)
+    return x.view(np.float16)
 
 
 def quantize_e4m3(w16: np.ndarray, scale_mode: int, layout: int = LAYOUT_KN):

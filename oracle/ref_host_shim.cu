@@ -15,6 +15,7 @@
 //   cpu_reference_fp16     :325-335
 //   cosine_stats           :337-355
 //   cpu_reference_scaled   :470-482
+//   fill_x (checkreal's synthetic activations) :408-413
 //   cpu_reference (fp16)   kernels/gemv_fp16.cu:287-297
 #include <cstdio>
 #include <cstdlib>
@@ -55,6 +56,12 @@ void ref_fill_host(uint16_t* W, size_t w_elems, uint16_t* x, int K, int N) {
   std::vector<__half> w(w_elems), xv(K);
   ref8::fill_host(w, xv, K, N);
   std::memcpy(W, w.data(), w_elems * sizeof(uint16_t));
+  std::memcpy(x, xv.data(), (size_t)K * sizeof(uint16_t));
+}
+
+void ref_fill_x(uint16_t* x, int K, unsigned seed) {
+  std::vector<__half> xv(K);
+  ref8::fill_x(xv, K, seed);
   std::memcpy(x, xv.data(), (size_t)K * sizeof(uint16_t));
 }
 

@@ -25,6 +25,8 @@ Fixtures written (all small, committed):
 * ``cfg0_fp16.npz``     -- FP16 GEMV K=3072 N=8192 M=1 on W ~ N(0,0.02),
   x ~ N(0,1) from numpy seed 0: sha256 of W and x, and the fp64 output of the
   reference's gemv_fp16.cu cpu_reference() (kernels/gemv_fp16.cu:287-297).
+* ``checkreal_x.npz``   -- checkreal's synthetic activations (fill_x,
+  kernels/gemv_fp8.cu:408-413) for K = 3072 and 8192 at seeds 1234 and 7.
 """
 from __future__ import annotations
 
@@ -144,6 +146,18 @@ def cfg0():
     print("cfg0_fp16: y", y.shape)
 
 
+def checkreal_x():
+    R = orc.ref()
+    out = {}
+    for K in (3072, 8192):
+        for seed in (1234, 7):
+            x = np.empty(K, np.uint16)
+            R.ref_fill_x(x, K, seed)
+            out[f"K{K}_s{seed}"] = x
+    np.savez_compressed(OUT / "checkreal_x.npz", **out)
+    print("checkreal_x:", sorted(out))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="the reference checkout")
@@ -155,6 +169,7 @@ def main():
     ref_small()
     ref_full()
     cfg0()
+    checkreal_x()
 
 
 if __name__ == "__main__":

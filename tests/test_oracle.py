@@ -198,3 +198,12 @@ def test_rmsnorm_silu_and_tp_restatement(orc, syn):
     h1 = orc.mlp_layer(h, layer)
     h2 = orc.mlp_layer_tp(h, layer, tp=4)
     assert orc.compare(h2, h1.astype(np.float64))["rel_l2"] < 2e-3
+
+
+def test_checkreal_x_matches_reference(orc):
+    """checkreal's synthetic activations (kernels/gemv_fp8.cu:408-413) as the
+    reference's own fill_x draws them."""
+    z = np.load(GOLDEN / "checkreal_x.npz")
+    for K in (3072, 8192):
+        for seed in (1234, 7):
+            assert np.array_equal(orc.fill_x_ref(K, seed).view(np.uint16), z[f"K{K}_s{seed}"]), (K, seed)
