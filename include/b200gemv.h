@@ -142,9 +142,17 @@ b2g_status b2g_destroy(b2g_op* op);
  *    split, up to one tile of imbalance); AUTO (default) = TILES when K is
  *    not split and the imbalance is at most 20%, else UNITS.
  *  B2G_OPT_KSPLIT: number of K ranges (0 = automatic).  Changes the packed
- *    layout: set it before b2g_prepack. */
-enum { B2G_OPT_MATH = 1, B2G_OPT_GRID = 2, B2G_OPT_PARTITION = 3, B2G_OPT_KSPLIT = 4 };
+ *    layout: set it before b2g_prepack.
+ *  B2G_OPT_PIPE: how the weights reach the math: REGISTERS = each warp
+ *    streams its units into a register ring with 16-byte loads; TMA = one
+ *    warp streams the CTA's range into a shared-memory ring of 16 KB stages
+ *    with 1-D bulk copies, 16 warps compute from it (tensor-core math only;
+ *    ops whose x rows leave fewer than two stages of shared memory stay on
+ *    REGISTERS).  AUTO (default) picks per shape.  The packed layout is the
+ *    same for both. */
+enum { B2G_OPT_MATH = 1, B2G_OPT_GRID = 2, B2G_OPT_PARTITION = 3, B2G_OPT_KSPLIT = 4, B2G_OPT_PIPE = 5 };
 enum { B2G_PARTITION_AUTO = 0, B2G_PARTITION_UNITS = 1, B2G_PARTITION_TILES = 2 };
+enum { B2G_PIPE_AUTO = 0, B2G_PIPE_REGISTERS = 1, B2G_PIPE_TMA = 2 };
 b2g_status b2g_op_set_option(b2g_op* op, int32_t key, int32_t value);
 
 /* The launch plan chosen for calls with m rows. */
@@ -162,6 +170,9 @@ typedef struct {
   int32_t n_slots;          /* virtual tiles per CTA (max) */
   int32_t x_kblocks;        /* 32-wide k blocks of x staged per CTA */
   int32_t math;
+  int32_t pipe;             /* B2G_PIPE_REGISTERS or _TMA, as planned for m */
+  int32_t n_stages;         /* TMA pipeline: ring stages (0 otherwise) */
+  int32_t stage_bytes;      /* TMA pipeline: bytes per stage (0 otherwise) */
 } b2g_plan_info;
 b2g_status b2g_op_query(const b2g_op* op, int32_t m, b2g_plan_info* info);
 /* The plan b2g_create would make on a GPU with num_sms SMs and smem_optin
@@ -336,10 +347,15 @@ b2g_status b2g_stack_workspace_init(const b2g_stack* st, void* workspace, b2g_st
  *  PERSISTENT: one cooperative launch runs every layer (up to 32 layers per
  *    launch), grid barriers between the gate||up and down phases; each
  *    phase's first weights are loaded while the barrier completes.
- * Both give bitwise-identical results; on B200 PER_LAYER is currently the
- * faster of the two (see the benchmark's detail output). */
+ *  PERSISTENT_TMA: one cooperative launch as PERSISTENT, the weights on the
+ *    TMA pipeline (B2G_OPT_PIPE): in each CTA one warp streams every phase's
+ *    range, layer after layer, through a shared-memory ring and asks L2 for
+ *    the phase after it, while 16 warps compute; the grid barriers involve
+ *    the computing warps only, so the weight stream runs through them.
+ * All modes give bitwise-identical results (see the benchmark's detail
+ * output for their speeds on B200). */
 enum { B2G_STACK_OPT_MODE = 1 };
-enum { B2G_STACK_MODE_PERSISTENT = 0, B2G_STACK_MODE_PER_LAYER = 1 };
+enum { B2G_STACK_MODE_PERSISTENT = 0, B2G_STACK_MODE_PER_LAYER = 1, B2G_STACK_MODE_PERSISTENT_TMA = 2 };
 b2g_status b2g_stack_set_option(b2g_stack* st, int32_t key, int32_t value);
 /* h [m, hidden] fp16 is read and overwritten; act is [m, intermediate] fp16
  * scratch.  The workspace must have been zeroed once by

@@ -25,11 +25,12 @@ DTYPE = {"fp16": 0, "fp8_e4m3": 1}
 SCALE = {"none": 0, "tensor_fp16": 1, "channel_fp16": 2, "channel_fp32": 3}
 LAYOUT = {"KN": 0, "NK": 1}
 FUSE_NONE, FUSE_GATE_UP_SILU, FUSE_RMSNORM_INPUT, FUSE_RESIDUAL_ADD = 0, 1, 2, 4
-OPT_MATH, OPT_GRID, OPT_PARTITION, OPT_KSPLIT = 1, 2, 3, 4
+OPT_MATH, OPT_GRID, OPT_PARTITION, OPT_KSPLIT, OPT_PIPE = 1, 2, 3, 4, 5
+PIPE_AUTO, PIPE_REGISTERS, PIPE_TMA = 0, 1, 2
 PARTITION_AUTO, PARTITION_UNITS, PARTITION_TILES = 0, 1, 2
 MATH_MMA, MATH_FFMA = 0, 1
 STACK_OPT_MODE = 1
-STACK_MODE_PERSISTENT, STACK_MODE_PER_LAYER = 0, 1
+STACK_MODE_PERSISTENT, STACK_MODE_PER_LAYER, STACK_MODE_PERSISTENT_TMA = 0, 1, 2
 
 
 class B2GError(RuntimeError):
@@ -59,7 +60,8 @@ class PlanInfo(ctypes.Structure):
                 ("total_units", ctypes.c_int64), ("unit_bytes", ctypes.c_int32),
                 ("inflight_bytes_per_cta", ctypes.c_int64), ("smem_bytes", ctypes.c_int64), ("max_contrib", ctypes.c_int32),
                 ("partition", ctypes.c_int32),
-                ("n_slots", ctypes.c_int32), ("x_kblocks", ctypes.c_int32), ("math", ctypes.c_int32)]
+                ("n_slots", ctypes.c_int32), ("x_kblocks", ctypes.c_int32), ("math", ctypes.c_int32),
+                ("pipe", ctypes.c_int32), ("n_stages", ctypes.c_int32), ("stage_bytes", ctypes.c_int32)]
 
     def as_dict(self):
         return {n: getattr(self, n) for n, _ in self._fields_}
@@ -357,9 +359,12 @@ class Stack:
             self.h = None
 
     def set_mode(self, mode):
-        """STACK_MODE_PERSISTENT (one cooperative launch) or STACK_MODE_PER_LAYER."""
+        """"per_layer" (two chained launches per layer), "persistent" (one
+        cooperative launch) or "persistent_tma" (one cooperative launch, weights
+        through the TMA pipeline)."""
         check(lib().b2g_stack_set_option(self.h, STACK_OPT_MODE, _code(
-            {"persistent": STACK_MODE_PERSISTENT, "per_layer": STACK_MODE_PER_LAYER}, mode)),
+            {"persistent": STACK_MODE_PERSISTENT, "per_layer": STACK_MODE_PER_LAYER,
+             "persistent_tma": STACK_MODE_PERSISTENT_TMA}, mode)),
             "b2g_stack_set_option")
 
     def set_layer(self, layer, packed_gu, scales_gu, packed_d, scales_d):

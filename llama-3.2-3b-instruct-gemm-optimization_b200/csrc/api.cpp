@@ -32,6 +32,7 @@ struct b2g_op {
   long long total_gran;
   int max_contrib, n_slots, xk_cap;
   int math;
+  int pipe;  // B2G_PIPE_* requested
 };
 
 struct b2g_stack {
@@ -62,6 +63,9 @@ int* g_err_word[64];
 // on 96): 64 KB 26.2 us, 128 KB 26.5, 256 KB 25.9, whole ranges 26.1 at
 // M = 8; 25.3 / 25.7 / 24.4 / 24.5 at M = 1.
 constexpr int kPrefetchBytesPerCta = 256 * 1024;
+// The TMA pipeline issues its prefetch once its own copies are all issued,
+// and asks for whole ranges (the next launch then streams from L2).
+constexpr int kPrefetchBytesTma = 1 << 30;
 
 b2g_status ensure_device_setup(int dev, int smem_optin) {
   std::lock_guard<std::mutex> lk(g_mu);
@@ -129,6 +133,9 @@ void plan_partition(b2g_op* op) {
 struct LaunchPlan {
   int off_epi, off_x, x_rs;
   size_t smem;
+  // TMA pipeline: the weight ring after the x rows (0 stages: does not fit)
+  int off_ring, n_stages;
+  size_t smem_tma;
 };
 
 // Shared memory per CTA (one CTA per SM): flags, the per-warp partial slots,
@@ -145,7 +152,19 @@ bool plan_launch(const b2g_op* op, int m, LaunchPlan* lp) {
   lp->off_x = (int)(lp->off_epi + epi_bytes);
   lp->x_rs = x_rs;
   lp->smem = lp->off_x + xbytes;
+  // TMA pipeline: as many 16 KB stages as the rest of the opt-in shared
+  // memory holds (at least 2, at most kMaxStages).
+  lp->off_ring = (int)((lp->smem + 1023) / 1024 * 1024);
+  const long long room = (long long)op->smem_optin - lp->off_ring;
+  lp->n_stages = room >= 2LL * kStageBytes ? (int)std::min<long long>(kMaxStages, room / kStageBytes) : 0;
+  lp->smem_tma = (size_t)lp->off_ring + (size_t)lp->n_stages * kStageBytes;
   return lp->smem <= (size_t)op->smem_optin;
+}
+
+// Whether calls with m rows run on the TMA pipeline.
+bool use_tma(const b2g_op* op, const LaunchPlan& lp) {
+  if (op->math != kMathMma || lp.n_stages < 2) return false;
+  return op->pipe == B2G_PIPE_TMA;
 }
 
 // One planning pass for `want` CTAs.  *slots_full: the CTAs' ranges touch
@@ -377,6 +396,10 @@ static b2g_status set_option_unchecked(b2g_op* op, int32_t key, int32_t value) {
       if (value < B2G_PARTITION_AUTO || value > B2G_PARTITION_TILES) return B2G_ERR_INVALID;
       op->partition = value;
       return replan(op);
+    case B2G_OPT_PIPE:
+      if (value < B2G_PIPE_AUTO || value > B2G_PIPE_TMA) return B2G_ERR_INVALID;
+      op->pipe = value;
+      return replan(op);
     case B2G_OPT_KSPLIT: {
       const int ks = choose_ksplit(op, value);
       if (value < 0 || ks < 1) return B2G_ERR_INVALID;
@@ -406,6 +429,14 @@ b2g_status b2g_op_query(const b2g_op* op, int32_t m, b2g_plan_info* info) {
   info->n_slots = op->n_slots;
   info->x_kblocks = op->xk_cap;
   info->math = op->math;
+  const bool tma = use_tma(op, lp);
+  info->pipe = tma ? B2G_PIPE_TMA : B2G_PIPE_REGISTERS;
+  info->n_stages = tma ? lp.n_stages : 0;
+  info->stage_bytes = tma ? kStageBytes : 0;
+  if (tma) {
+    info->smem_bytes = (int64_t)lp.smem_tma;
+    info->inflight_bytes_per_cta = (int64_t)lp.n_stages * kStageBytes;
+  }
   return B2G_OK;
 }
 
@@ -518,9 +549,16 @@ static b2g_status enqueue_impl(const b2g_op* op, const b2g_enqueue_args* a, cons
     p.pf_gran = nx->gran;
     p.pf_unit_bytes = nx->unit_bytes;
     p.pf_grid = nx->grid;
-    p.pf_bytes = kPrefetchBytesPerCta;
+    p.pf_bytes = use_tma(op, lp) ? kPrefetchBytesTma : kPrefetchBytesPerCta;
   }
   if (tp) p.tp = *tp;
+  if (use_tma(op, lp)) {
+    p.off_ring = lp.off_ring;
+    p.n_stages = lp.n_stages;
+    p.stage_bytes = kStageBytes;
+    return cuda_status(launch_gemv_tma(p, op->planes, op->wbytes, lp.smem_tma, a->pdl != 0,
+                                       reinterpret_cast<cudaStream_t>(stream)));
+  }
   return cuda_status(launch_gemv(p, op->planes, op->wbytes, op->math, lp.smem, a->pdl != 0,
                                  reinterpret_cast<cudaStream_t>(stream)));
 }
@@ -833,7 +871,9 @@ b2g_status b2g_stack_workspace_init(const b2g_stack* st, void* ws, b2g_stream_t 
 b2g_status b2g_stack_set_option(b2g_stack* st, int32_t key, int32_t value) {
   if (!st) return B2G_ERR_INVALID;
   if (key != B2G_STACK_OPT_MODE) return B2G_ERR_INVALID;
-  if (value != B2G_STACK_MODE_PERSISTENT && value != B2G_STACK_MODE_PER_LAYER) return B2G_ERR_INVALID;
+  if (value != B2G_STACK_MODE_PERSISTENT && value != B2G_STACK_MODE_PER_LAYER &&
+      value != B2G_STACK_MODE_PERSISTENT_TMA)
+    return B2G_ERR_INVALID;
   st->mode = value;
   return B2G_OK;
 }
@@ -878,6 +918,56 @@ static b2g_status stack_enqueue_persistent(const b2g_stack* st, int32_t m, void*
   return B2G_OK;
 }
 
+// All layers in cooperative launches of the TMA-pipeline stack kernel: one
+// ring after the larger of the two phases' shared-memory layouts.
+static b2g_status stack_enqueue_tma(const b2g_stack* st, int32_t m, void* h, void* act, void* ws,
+                                    cudaStream_t stream) {
+  const b2g_op* gu = st->gu;
+  const b2g_op* dn = st->dn;
+  if (gu->wbytes != dn->wbytes || gu->math != kMathMma || dn->math != kMathMma) return B2G_ERR_UNSUPPORTED;
+  const int grid = std::max(gu->grid, dn->grid);
+  if (!aligned(ws, 16) || !aligned(h, 2) || !aligned(act, 2)) return B2G_ERR_INVALID;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B2G_ERR_CUDA;
+  if (dev != gu->device) return B2G_ERR_INVALID;
+  b2g_status s = ensure_device_setup(dev, gu->smem_optin);
+  if (s != B2G_OK) return s;
+  LaunchPlan lg, ld;
+  if (!plan_launch(gu, m, &lg) || !plan_launch(dn, m, &ld)) return B2G_ERR_OOM;
+  const int off_ring = std::max(lg.off_ring, ld.off_ring);
+  const long long room = (long long)gu->smem_optin - off_ring;
+  const int n_stages = (int)std::min<long long>(kMaxStages, room / kStageBytes);
+  if (n_stages < 2) return B2G_ERR_UNSUPPORTED;
+  const size_t smem = (size_t)off_ring + (size_t)n_stages * kStageBytes;
+  int max_grid = 0;
+  if (stack_tma_max_coresident(gu->wbytes, smem, gu->num_sms, &max_grid) != cudaSuccess) return B2G_ERR_CUDA;
+  if (grid > max_grid) return B2G_ERR_UNSUPPORTED;
+  StackParams sp = {};
+  fill_plan(gu, m, lg, ws, dev, &sp.gu);
+  fill_plan(dn, m, ld, ws, dev, &sp.dn);
+  for (GemvParams* p : {&sp.gu, &sp.dn}) {
+    p->off_ring = off_ring;
+    p->n_stages = n_stages;
+    p->stage_bytes = kStageBytes;
+  }
+  sp.gu.rms_eps = st->f.rms_eps;
+  sp.h = static_cast<__half*>(h);
+  sp.ldh = st->f.hidden;
+  sp.act = static_cast<__half*>(act);
+  sp.ldact = st->f.intermediate;
+  sp.barrier = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + kBarrierWordOffset);
+  for (int l0 = 0; l0 < st->f.n_layers; l0 += kMaxStackLayers) {
+    sp.n_layers = std::min(kMaxStackLayers, st->f.n_layers - l0);
+    for (int i = 0; i < sp.n_layers; ++i) {
+      const auto& L = st->layers[l0 + i];
+      sp.layers[i] = StackLayer{static_cast<const uint8_t*>(L.pgu), L.sgu, static_cast<const uint8_t*>(L.pd),
+                                L.sd};
+    }
+    if (launch_stack_tma(sp, grid, gu->wbytes, smem, stream) != cudaSuccess) return B2G_ERR_CUDA;
+  }
+  return B2G_OK;
+}
+
 b2g_status b2g_stack_enqueue(const b2g_stack* st, int32_t m, void* h, void* act, void* ws, b2g_stream_t stream) {
   if (!st || !h || !act || !ws) return B2G_ERR_INVALID;
   if (m < 1 || m > st->f.max_m) return B2G_ERR_INVALID;
@@ -888,10 +978,13 @@ b2g_status b2g_stack_enqueue(const b2g_stack* st, int32_t m, void* h, void* act,
     if (st->f.scale_mode == B2G_SCALE_CHANNEL_FP32 && (!aligned(L.sgu, 4) || !aligned(L.sd, 4)))
       return B2G_ERR_INVALID;
   }
-  if (st->mode == B2G_STACK_MODE_PERSISTENT) {
-    // Shapes whose two phases plan different grids, or a grid that cannot be
-    // co-resident, run per layer instead.
-    const b2g_status s = stack_enqueue_persistent(st, m, h, act, ws, reinterpret_cast<cudaStream_t>(stream));
+  if (st->mode == B2G_STACK_MODE_PERSISTENT || st->mode == B2G_STACK_MODE_PERSISTENT_TMA) {
+    // A grid that cannot be co-resident (or a ring that does not fit) runs
+    // per layer instead.
+    const b2g_status s =
+        st->mode == B2G_STACK_MODE_PERSISTENT
+            ? stack_enqueue_persistent(st, m, h, act, ws, reinterpret_cast<cudaStream_t>(stream))
+            : stack_enqueue_tma(st, m, h, act, ws, reinterpret_cast<cudaStream_t>(stream));
     if (s != B2G_ERR_UNSUPPORTED) return s;
   }
   for (int l = 0; l < st->f.n_layers; ++l) {

@@ -140,6 +140,35 @@ __device__ __forceinline__ Epi epi_of(const GemvParams& p, uint8_t* smem, int P)
   return Epi{base, base + p.n_slots * P * 16};
 }
 
+// The scales of the CTA's tiles (constants: may load before the previous
+// kernel is waited on).
+template <int P>
+__device__ __forceinline__ void load_scales(const GemvParams& p, const Io& io, const Epi& e, int vt_first, int nvt,
+                                            int tid) {
+  const int ns = nvt * P * 16;
+  for (int i = tid; i < ns; i += NT) {
+    const int j = i / (P * 16), pl = (i / 16) % P, c = i % 16;
+    const int tile = fdiv(vt_first + j, p.div_tiles);
+    const int n = (vt_first + j - tile * p.n_tiles) * kTileCh + c;
+    e.scale[i] = n < p.N ? channel_scale(p, io, pl, n) : 0.f;
+  }
+}
+
+// The residual rows of the CTA's tiles (written by an earlier kernel or phase).
+template <int P>
+__device__ __forceinline__ void load_residual(const GemvParams& p, const Io& io, const Epi& e, int vt_first,
+                                              int nvt, int tid) {
+  if (P == 1 && p.residual_add) {
+    const int nr = nvt * 8 * 16;
+    for (int i = tid; i < nr; i += NT) {
+      const int j = i / 128, m = (i / 16) % 8, c = i % 16;
+      const int vt = vt_first + j;
+      const int n = (vt - fdiv(vt, p.div_tiles) * p.n_tiles) * kTileCh + c;
+      e.res[i] = (m < p.M && n < p.N) ? __half2float(__ldcg(io.residual + (size_t)m * io.ldr + n)) : 0.f;
+    }
+  }
+}
+
 template <int P>
 __device__ __forceinline__ void load_epi(const GemvParams& p, const Io& io, const Epi& e, int vt_first, int nvt,
                                          int tid) {
@@ -428,10 +457,12 @@ __device__ __forceinline__ uint4 tp_sum8(const TpParams& tp, int m, int k0) {
 // assignment, layout and sums of squares as stage_x (so the norm is bitwise
 // the plain path's); rows are whole (k_lo = 0, host-checked).  Rows go in
 // batches of 4, every rank's slot load of a batch issued before its sums.
-__device__ void gather_x(const GemvParams& p, __half* xs, int krange, int tid, float* red, volatile int* verdict) {
+template <class Sync>
+__device__ void gather_x(const GemvParams& p, __half* xs, int krange, int tid, float* red, volatile int* verdict,
+                         Sync sync) {
   const int M = p.M;
   if (tid == 0) *verdict = tp_wait_arrivals(p.tp, p.error) ? 1 : 0;
-  __syncthreads();
+  sync();
   const int nch = krange / 8;
   constexpr int B = 4;
   float ss[8];
@@ -699,7 +730,7 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
   if (gather) {
     // every CTA takes part (the wait and the write-back of the reduced rows)
     gather_x(p, xs, active ? krange : p.K / 8 * 8, tid, p.rmsnorm ? red : nullptr,
-             reinterpret_cast<volatile int*>(smem + kOffMisc));
+             reinterpret_cast<volatile int*>(smem + kOffMisc), [] { __syncthreads(); });
   }
   if (active) {
     if (!gather) stage_x(p, io, xs, k_lo, krange, tid, p.rmsnorm ? red : nullptr);
@@ -870,6 +901,312 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_
   if (tid == 0) TRACE(4);
 }
 
+
+// ---------------------------------------------------------------------------
+// TMA pipeline: weights through a ring of stages in shared memory
+// ---------------------------------------------------------------------------
+// Warp 16 (lane 0, the producer) streams a CTA's contiguous range of the
+// packed weights into a ring of n_stages stages with 1-D bulk copies
+// (cp.async.bulk from this GPU's memory; no multicast).  Warps 0..15 (the
+// consumers) take the units as the register-ring kernel does (warp w: units
+// w, w + 16, ... of the range) and read each lane's 16-byte A fragment from
+// the ring.  Stage s of the ring's life fills slot s % n_stages; full[slot]
+// completes when its bytes land, empty[slot] when all 16 consumer warps have
+// passed it.  The copies never wait for activations: while the consumers
+// wait for the previous kernel (or grid phase) and stage x, the ring fills.
+__device__ __forceinline__ void consumer_sync() { named_sync(1, kThreads); }
+
+struct Ring {
+  uint8_t* base;
+  uint64_t* full;
+  uint64_t* empty;
+  int n_stages, stage_bytes;
+  int slot;        // next stage's slot
+  uint32_t round;  // times the ring has wrapped before the next stage
+  __device__ __forceinline__ void advance() {
+    if (++slot == n_stages) {
+      slot = 0;
+      ++round;
+    }
+  }
+};
+
+__device__ __forceinline__ Ring ring_at(uint8_t* smem, int off_ring, int n_stages, int stage_bytes) {
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBars);
+  return Ring{smem + off_ring, full, full + kMaxStages, n_stages, stage_bytes, 0, 0u};
+}
+
+// Thread 0 of a CTA: the ring's mbarriers (followed by a CTA-wide barrier).
+__device__ __forceinline__ void ring_init(const Ring& r) {
+  for (int i = 0; i < r.n_stages; ++i) {
+    mbar_init(&r.full[i], 1);
+    mbar_init(&r.empty[i], W);
+  }
+  fence_mbarrier_init();
+}
+
+// Producer: units [u0, u1) of `packed` into the next stages.  False if a
+// wait for a free slot expired (the error word is set; nothing more is issued).
+__device__ bool ring_produce(Ring& r, const uint8_t* packed, int unit_bytes, int u0, int u1, uint64_t pol,
+                             int* err) {
+  const long long all = (long long)(u1 - u0) * unit_bytes;
+  const uint8_t* src = packed + (size_t)u0 * unit_bytes;
+  for (long long off = 0; off < all; off += r.stage_bytes) {
+    if (r.round > 0 && !mbar_wait_bounded(&r.empty[r.slot], (r.round - 1) & 1)) {
+      atomicCAS(err, 0, kErrEmptyWait);
+      return false;
+    }
+    const uint32_t bytes = (uint32_t)min((long long)r.stage_bytes, all - off);
+    mbar_arrive_expect_tx(&r.full[r.slot], bytes);
+    bulk_g2s(r.base + (size_t)r.slot * r.stage_bytes, src + off, bytes, &r.full[r.slot], pol);
+    r.advance();
+  }
+  return true;
+}
+
+// Producer, before it leaves: every stage it issued has landed (bounded), so
+// no copy into this CTA's shared memory is in flight once it exits.
+__device__ void ring_drain(const Ring& r, long long issued, int* err) {
+  Ring q = r;
+  for (long long i = 0; i < min(issued, (long long)r.n_stages); ++i) {
+    if (q.slot == 0) {
+      q.slot = r.n_stages - 1;
+      --q.round;
+    } else {
+      --q.slot;
+    }
+    if (!mbar_wait_bounded(&q.full[q.slot], q.round & 1)) {
+      atomicCAS(err, 0, kErrDrainWait);
+      return;
+    }
+  }
+}
+
+// L2 prefetch of CTA c's range of a partition (units of unit_bytes in
+// granules of gran over `grid` CTAs), up to `bytes`.
+__device__ __forceinline__ void l2_prefetch_range(const uint8_t* packed, long long total_units, int gran,
+                                                  int unit_bytes, int grid, int c, long long bytes) {
+  const long long tg = total_units / gran;
+  const long long a = (long long)c * tg / grid * gran;
+  const long long b = (long long)(c + 1) * tg / grid * gran;
+  bytes = min(bytes, (b - a) * unit_bytes);
+  const uint8_t* src = packed + a * unit_bytes;
+  for (long long off = 0; off < bytes; off += 32768) bulk_prefetch_l2(src + off, (uint32_t)min(32768LL, bytes - off));
+}
+
+struct Geom {
+  Range r;
+  bool active;
+  int vt_first, vt_last, k_lo, krange;
+};
+
+template <int WB>
+__device__ __forceinline__ Geom geom_of(const GemvParams& p, int warp) {
+  constexpr int KPB = (WB == 1) ? 32 : 16;
+  Geom g;
+  g.r = cta_range(p, warp);
+  g.active = g.r.u1 > g.r.u0;
+  g.vt_first = fdiv(g.r.u0, p.div_kbpv);
+  g.vt_last = g.active ? fdiv(g.r.u1 - 1, p.div_kbpv) : g.vt_first - 1;
+  const int ks_first = fdiv(g.vt_first, p.div_tiles);
+  g.k_lo = ks_first * p.kbpv * KPB;
+  g.krange = g.active ? (fdiv(g.vt_last, p.div_tiles) + 1 - ks_first) * p.kbpv * KPB : 0;
+  return g;
+}
+
+// Consumers, before the activations exist: zeroed partial slots, the scales.
+template <int P>
+__device__ __forceinline__ void tma_setup(const GemvParams& p, const Io& io, uint8_t* smem, const Geom& g, int tid) {
+  float4* slots = reinterpret_cast<float4*>(smem + kOffSlots);
+  for (int i = tid; i < p.n_slots * W * P * 32; i += NT) slots[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (g.active) load_scales<P>(p, io, epi_of(p, smem, P), g.vt_first, g.vt_last - g.vt_first + 1, tid);
+}
+
+// Consumers, once the activations exist: x (staged, or all-reduced by the
+// tensor-parallel gather), the residual rows; a consumer barrier at the end.
+template <int P, bool TPX>
+__device__ __forceinline__ void tma_inputs(const GemvParams& p, const Io& io, uint8_t* smem, const Geom& g, int tid) {
+  float* red = reinterpret_cast<float*>(smem + kOffRed);
+  __half* xs = reinterpret_cast<__half*>(smem + p.off_x);
+  if (TPX && p.tp.mode == kTpGather) {
+    gather_x(p, xs, g.active ? g.krange : p.K / 8 * 8, tid, p.rmsnorm ? red : nullptr,
+             reinterpret_cast<volatile int*>(smem + kOffMisc), [] { consumer_sync(); });
+  } else if (g.active) {
+    stage_x(p, io, xs, g.k_lo, g.krange, tid, p.rmsnorm ? red : nullptr);
+  }
+  if (g.active) load_residual<P>(p, io, epi_of(p, smem, P), g.vt_first, g.vt_last - g.vt_first + 1, tid);
+  consumer_sync();
+}
+
+// Consumers: this CTA's range from the ring (every stage of it, in order:
+// every warp waits for and then releases every stage, so the producer can
+// refill it), then the combine and the epilogue.
+template <int P, int WB, bool TPX>
+__device__ void tma_stream(const GemvParams& p, const Io& io, uint8_t* smem, const Geom& geo, Ring& ring, bool& live,
+                           int trace_base = -1) {
+  constexpr int UNIT = P * kUnitPlaneBytes;
+  constexpr int KPB = (WB == 1) ? 32 : 16;
+  float* red = reinterpret_cast<float*>(smem + kOffRed);
+  const Epi epi = epi_of(p, smem, P);
+  float4* slots = reinterpret_cast<float4*>(smem + kOffSlots);  // [n_slots][W][P][32]
+  __half* xs = reinterpret_cast<__half*>(smem + p.off_x);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int M = p.M, kbpv = p.kbpv;
+  const int u0 = geo.r.u0, n_mine = geo.r.n_mine;
+  const int vt_first = geo.vt_first, k_lo = geo.k_lo;
+  const int nvt = geo.vt_last - vt_first + 1;
+  const int SU = ring.stage_bytes / UNIT;  // units per stage (a multiple of 16)
+  const int UPW = SU / W;                  // each warp's units per full stage
+  const int n_st = (geo.r.u1 - geo.r.u0 + SU - 1) / SU;
+  if (tid == 0) STRACE(trace_base + 1);
+
+  MmaMath<P, WB> math;
+  math.zero();
+  int vt = fdiv(u0 + warp, p.div_kbpv);
+  int kbl = (u0 + warp) - vt * kbpv;
+  int seg_n = (kbpv - kbl + W - 1) / W;
+  int seg_left = seg_n;
+  int cur_j = vt - vt_first;
+  const __half* xlane = xs + (size_t)(g < M ? g : 0) * p.x_rs + (WB == 1 ? 8 * q : 4 * q);
+  int xoff = (fdiv(vt, p.div_tiles) * kbpv + kbl) * KPB - k_lo;
+  uint32_t xa = smem_addr(xlane) + 2 * xoff;
+  const uint32_t wbase = smem_addr(ring.base) + warp * UNIT + lane * 16;
+  auto flush = [&](int j) {
+    float v[P][4];
+    math.result(v, lane);
+#pragma unroll
+    for (int pl = 0; pl < P; ++pl)
+      slots[((size_t)(j * W + warp) * P + pl) * 32 + lane] = make_float4(v[pl][0], v[pl][1], v[pl][2], v[pl][3]);
+  };
+  int j = 0;
+#pragma unroll 1
+  for (int s = 0; s < n_st; ++s) {
+    const int jend = min((s + 1) * UPW, n_mine);
+    // Every warp waits for every stage, even one it has no units in (the
+    // last stage of a range may be short): its arrival on empty must count
+    // for this round of the slot, which has begun only once the producer
+    // has refilled it.
+    if (live && !mbar_wait_bounded(&ring.full[ring.slot], ring.round & 1)) {
+      atomicCAS(p.error, 0, kErrFullWait);
+      live = false;
+    }
+    const uint32_t sa = wbase + (uint32_t)(ring.slot * ring.stage_bytes);
+#pragma unroll 1
+    for (int k = 0; j < jend; ++j, ++k) {
+      uint4 w[P];
+#pragma unroll
+      for (int pl = 0; pl < P; ++pl) w[pl] = lds128_at(sa + (uint32_t)(k * W * UNIT + pl * kUnitPlaneBytes));
+      uint4 xf;
+      if constexpr (WB == 1) {
+        xf = lds128_at(xa);
+      } else {
+        const uint2 t = lds64_at(xa);
+        xf = make_uint4(t.x, t.y, 0u, 0u);
+      }
+      math.unit(w, xf);
+      xoff += W * KPB;
+      xa += 2 * W * KPB;
+      if (--seg_left == 0) {
+        flush(cur_j);
+        math.zero();
+        kbl += seg_n * W - kbpv;
+        ++vt;
+        while (kbl >= kbpv) {
+          kbl -= kbpv;
+          ++vt;
+        }
+        seg_n = (kbpv - kbl + W - 1) / W;
+        seg_left = seg_n;
+        cur_j = vt - vt_first;
+        xoff = (fdiv(vt, p.div_tiles) * kbpv + kbl) * KPB - k_lo;
+        xa = smem_addr(xlane) + 2 * xoff;
+      }
+    }
+    // this warp is done with the stage: one arrival frees the slot
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ring.empty[ring.slot]);
+    ring.advance();
+  }
+  if (n_mine > 0 && seg_left != seg_n) flush(cur_j);
+  if (tid == 0) STRACE(trace_base + 2);
+
+  // ---- combine the warps' partials in warp order, then finish each tile
+  consumer_sync();
+  for (int jj = warp; jj < nvt; jj += W) {
+    float v[P][4];
+#pragma unroll
+    for (int pl = 0; pl < P; ++pl) v[pl][0] = v[pl][1] = v[pl][2] = v[pl][3] = 0.f;
+#pragma unroll
+    for (int w2 = 0; w2 < W; ++w2) {
+#pragma unroll
+      for (int pl = 0; pl < P; ++pl) {
+        const float4 t = slots[((size_t)(jj * W + w2) * P + pl) * 32 + lane];
+        v[pl][0] += t.x;
+        v[pl][1] += t.y;
+        v[pl][2] += t.z;
+        v[pl][3] += t.w;
+      }
+    }
+    __syncwarp();
+    finish_vt<P, TPX>(p, io, vt_first + jj, jj, v, lane, p.rmsnorm ? red : nullptr, epi,
+                      reinterpret_cast<__half*>(slots + (size_t)jj * W * P * 32));
+  }
+  if (tid == 0) STRACE(trace_base + 3);
+}
+
+// ---------------------------------------------------------------------------
+// One GEMV per launch on the TMA pipeline
+// ---------------------------------------------------------------------------
+template <int P, int WB, bool TPX>
+__global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(const __grid_constant__ GemvParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  constexpr int UNIT = P * kUnitPlaneBytes;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  Ring ring = ring_at(smem, p.off_ring, p.n_stages, p.stage_bytes);
+  if (tid == 0) ring_init(ring);
+  __syncthreads();  // the barriers are initialised before anyone uses them
+  pdl_launch_dependents();
+  if (warp == W) {
+    // ---- producer: weights are constant, so no dependency wait
+    if (lane == 0) {
+      const Range rg = cta_range(p, 0);
+      ring_produce(ring, p.packed, UNIT, rg.u0, rg.u1, l2_policy_evict_first(), p.error);
+      // Every copy of this range is issued: HBM goes on with the next
+      // kernel's weights (the ranges its CTAs blockIdx.x, blockIdx.x + grid,
+      // ... will stream) while this kernel's math, its epilogue, the launch
+      // gap and the next kernel's activation staging run.
+      if (p.pf_packed != nullptr)
+        for (int c = blockIdx.x; c < p.pf_grid; c += p.grid)
+          l2_prefetch_range(p.pf_packed, p.pf_total_units, p.pf_gran, p.pf_unit_bytes, p.pf_grid, c, p.pf_bytes);
+      ring_drain(ring, (long long)ring.round * ring.n_stages + ring.slot, p.error);
+    }
+    return;
+  }
+  // ---- consumers (warps 0..15)
+  if (tid == 0) TRACE(0);
+  const Io io = io_of_params(p);
+  const Geom geo = geom_of<WB>(p, warp);
+  tma_setup<P>(p, io, smem, geo, tid);
+  pdl_wait();
+  if (tid == 0) TRACE(1);
+  if (TPX && p.tp.mode == kTpPush && blockIdx.x == 0 && tid == 0) atomicAdd(p.tp.epoch, 1u);
+  tma_inputs<P, TPX>(p, io, smem, geo, tid);
+  if (tid == 0) TRACE(2);
+  bool live = true;
+  tma_stream<P, WB, TPX>(p, io, smem, geo, ring, live);
+  if (tid == 0) TRACE(3);
+  if (TPX && p.tp.mode == kTpPush) {
+    // This CTA's peer stores are done: one arrival on every rank.
+    consumer_sync();
+    if (tid == 0) {
+      fence_acq_rel_sys();
+      for (int r = 0; r < p.tp.world; ++r) red_relaxed_sys_add(p.tp.counters[r] + p.tp.rank, 1u);
+    }
+  }
+  if (tid == 0) TRACE(4);
+}
+
 // ---------------------------------------------------------------------------
 // The decode-MLP stack in one cooperative launch
 // ---------------------------------------------------------------------------
@@ -958,6 +1295,107 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
   if (tid == 0) TRACE(4);
 }
 
+
+// ---------------------------------------------------------------------------
+// The decode-MLP stack in one cooperative launch on the TMA pipeline
+// ---------------------------------------------------------------------------
+// The producer streams every phase's range of this CTA in order -- layer l's
+// gate||up, then its down, then layer l + 1's gate||up ... -- through one
+// ring, bounded only by free slots, and asks L2 for the phase after the one
+// it streams (so HBM keeps working while the consumers sit at a grid barrier
+// or stage activations).  The consumers run the phases; a grid barrier
+// (consumer threads only) separates each phase from the next, since every
+// tile of a phase reads all of the previous phase's rows.
+__device__ __forceinline__ void cgrid_arrive(unsigned* counter) {
+  if (threadIdx.x == 0) {
+    fence_acq_rel_gpu();  // this CTA's rows (ordered by the consumer barrier) before the arrival
+    atomicAdd(counter, 1u);
+  }
+}
+
+// Waits (thread 0, bounded) until the counter reaches target, then releases
+// the consumers.  False once a wait expired (or the error word was already
+// set); the phase still runs, on void data.
+__device__ __forceinline__ bool cgrid_wait(unsigned* counter, unsigned target, int* err, volatile int* verdict) {
+  if (threadIdx.x == 0) {
+    int ok = *reinterpret_cast<volatile int*>(err) == 0;
+    const unsigned long long t0 = globaltimer_ns();
+    while (ok) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
+      if (v >= target) break;
+      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+        atomicCAS(err, 0, kErrGridWait);
+        ok = 0;
+      }
+      __nanosleep(32);
+    }
+    *verdict = ok;
+  }
+  consumer_sync();
+  return *verdict != 0;
+}
+
+template <int WB>
+__global__ void __launch_bounds__(kTmaThreads, 1) stack_tma_kernel(const __grid_constant__ StackParams sp) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const GemvParams& gu = sp.gu;
+  const GemvParams& dn = sp.dn;
+  const unsigned G = gridDim.x;
+  Ring ring = ring_at(smem, gu.off_ring, gu.n_stages, gu.stage_bytes);
+  if (tid == 0) ring_init(ring);
+  __syncthreads();
+  if (warp == W) {
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      const Range rg = cta_range(gu, 0), rd = cta_range(dn, 0);
+      for (int l = 0; l < sp.n_layers; ++l) {
+        const StackLayer& L = sp.layers[l];
+        if (!ring_produce(ring, L.pgu, 2 * kUnitPlaneBytes, rg.u0, rg.u1, pol, gu.error)) break;
+        if (rd.u1 > rd.u0)
+          l2_prefetch_range(L.pd, dn.total_units, dn.gran, kUnitPlaneBytes, dn.grid, blockIdx.x, kWholeRange);
+        if (!ring_produce(ring, L.pd, kUnitPlaneBytes, rd.u0, rd.u1, pol, gu.error)) break;
+        if (l + 1 < sp.n_layers && rg.u1 > rg.u0)
+          l2_prefetch_range(sp.layers[l + 1].pgu, gu.total_units, gu.gran, 2 * kUnitPlaneBytes, gu.grid, blockIdx.x,
+                            kWholeRange);
+      }
+      ring_drain(ring, (long long)ring.round * ring.n_stages + ring.slot, gu.error);
+    }
+    return;
+  }
+  // ---- consumers
+  volatile int* verdict = reinterpret_cast<volatile int*>(smem + kOffMisc);
+  unsigned nbar = 0;
+  bool live = true;
+  for (int l = 0; l < sp.n_layers; ++l) {
+    const StackLayer& L = sp.layers[l];
+    // act = SiLU(RMSNorm(h) . Wg) * (RMSNorm(h) . Wu)
+    const Io io_gu{L.pgu, L.sgu, sp.h, sp.ldh, nullptr, 0, sp.act, sp.ldact};
+    const Geom g1 = geom_of<WB>(gu, warp);
+    if (tid == 0) STRACE(8 * l);
+    tma_setup<2>(gu, io_gu, smem, g1, tid);
+    if (l > 0) cgrid_wait(sp.barrier, (++nbar) * G, gu.error, verdict);
+    tma_inputs<2, false>(gu, io_gu, smem, g1, tid);
+    tma_stream<2, WB, false>(gu, io_gu, smem, g1, ring, live, 8 * l);
+    consumer_sync();
+    cgrid_arrive(sp.barrier);
+    // h = h + act . Wd
+    const Io io_dn{L.pd, L.sd, sp.act, sp.ldact, sp.h, sp.ldh, sp.h, sp.ldh};
+    const Geom g2 = geom_of<WB>(dn, warp);
+    if (tid == 0) STRACE(8 * l + 4);
+    tma_setup<1>(dn, io_dn, smem, g2, tid);
+    cgrid_wait(sp.barrier, (++nbar) * G, gu.error, verdict);
+    tma_inputs<1, false>(dn, io_dn, smem, g2, tid);
+    tma_stream<1, WB, false>(dn, io_dn, smem, g2, ring, live, 8 * l + 4);
+    if (l + 1 < sp.n_layers) {
+      consumer_sync();
+      cgrid_arrive(sp.barrier);
+    }
+  }
+  grid_exit(sp.barrier, (nbar + 1) * G);
+}
+
 template <int P, int WB, int MATH>
 cudaError_t launch_variant(const GemvParams& p, size_t smem, bool pdl, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
@@ -985,7 +1423,57 @@ cudaError_t launch_variant(const GemvParams& p, size_t smem, bool pdl, cudaStrea
   }
 }
 
+template <int P, int WB>
+cudaError_t launch_tma_variant(const GemvParams& p, size_t smem, bool pdl, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(kTmaThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  if (p.tp.mode != kTpNone) return cudaLaunchKernelEx(&cfg, gemv_tma_kernel<P, WB, true>, p);
+  return cudaLaunchKernelEx(&cfg, gemv_tma_kernel<P, WB, false>, p);
+}
+
 }  // namespace
+
+cudaError_t launch_gemv_tma(const GemvParams& p, int planes, int wbytes, size_t smem, bool pdl,
+                            cudaStream_t stream) {
+  if (planes == 1 && wbytes == 1) return launch_tma_variant<1, 1>(p, smem, pdl, stream);
+  if (planes == 2 && wbytes == 1) return launch_tma_variant<2, 1>(p, smem, pdl, stream);
+  if (planes == 1 && wbytes == 2) return launch_tma_variant<1, 2>(p, smem, pdl, stream);
+  if (planes == 2 && wbytes == 2) return launch_tma_variant<2, 2>(p, smem, pdl, stream);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_stack_tma(const StackParams& sp, int grid, int wbytes, size_t smem, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kTmaThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (wbytes == 1) return cudaLaunchKernelEx(&cfg, stack_tma_kernel<1>, sp);
+  if (wbytes == 2) return cudaLaunchKernelEx(&cfg, stack_tma_kernel<2>, sp);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t stack_tma_max_coresident(int wbytes, size_t smem, int num_sms, int* max_grid) {
+  int per_sm = 0;
+  const cudaError_t e =
+      wbytes == 1 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stack_tma_kernel<1>, kTmaThreads, smem)
+                  : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stack_tma_kernel<2>, kTmaThreads, smem);
+  *max_grid = per_sm * num_sms;
+  return e;
+}
 
 cudaError_t launch_gemv(const GemvParams& p, int planes, int wbytes, int math, size_t smem, bool pdl,
                         cudaStream_t stream) {
@@ -1076,6 +1564,16 @@ cudaError_t gemv_set_smem_limit(int bytes) {
   B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma, true>))
   B2G_LIM((stack_kernel<1>))
   B2G_LIM((stack_kernel<2>))
+  B2G_LIM((gemv_tma_kernel<1, 1, false>))
+  B2G_LIM((gemv_tma_kernel<1, 1, true>))
+  B2G_LIM((gemv_tma_kernel<2, 1, false>))
+  B2G_LIM((gemv_tma_kernel<2, 1, true>))
+  B2G_LIM((gemv_tma_kernel<1, 2, false>))
+  B2G_LIM((gemv_tma_kernel<1, 2, true>))
+  B2G_LIM((gemv_tma_kernel<2, 2, false>))
+  B2G_LIM((gemv_tma_kernel<2, 2, true>))
+  B2G_LIM((stack_tma_kernel<1>))
+  B2G_LIM((stack_tma_kernel<2>))
 #undef B2G_LIM
   return e;
 }

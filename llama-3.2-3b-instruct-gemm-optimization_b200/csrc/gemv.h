@@ -30,7 +30,13 @@ constexpr int kRing = 16;     // uint4 registers per lane for in-flight weight u
 // the x rows.
 constexpr int kOffMisc = 64;
 constexpr int kOffRed = 128;
+constexpr int kOffBars = 640;  // TMA pipeline: full[kMaxStages] then empty[kMaxStages] mbarriers
+constexpr int kMaxStages = 24;
 constexpr int kOffSlots = 1024;
+// TMA pipeline (gemv_tma_kernel): warps 0..15 compute, warp 16 streams the
+// weights into a ring of n_stages stages of stage_bytes in shared memory.
+constexpr int kTmaThreads = kThreads + 32;
+constexpr int kStageBytes = 16384;
 // Workspace: tile counters first (fixed size, so ops sharing one workspace
 // agree on where they are), then the split-K partials.  The last 256 bytes of
 // the counter region hold the stack kernel's grid-barrier counter.
@@ -115,6 +121,9 @@ struct GemvParams {
   int off_epi;    // shared-memory byte offset of the epilogue inputs
   int off_x;      // shared-memory byte offset of the x rows
   int x_rs;       // x row stride in shared memory (halves)
+  int off_ring;   // TMA pipeline: shared-memory byte offset of the weight ring
+  int n_stages;   // ring stages (<= kMaxStages)
+  int stage_bytes;
   // L2 prefetch of the next kernel's stream (pf_packed null = off): the
   // first pf_bytes of every range the next launch's CTAs will stream (its
   // partition: pf_total_units units of pf_unit_bytes in granules of pf_gran
@@ -135,6 +144,10 @@ cudaError_t launch_tp_gather(const TpParams& tp, int m, int* error, cudaStream_t
 // Launch one GEMV (planes = 1 or 2, wbytes = 1 for E4M3 or 2 for FP16).
 cudaError_t launch_gemv(const GemvParams& p, int planes, int wbytes, int math, size_t smem,
                         bool pdl, cudaStream_t stream);
+// The same GEMV with the weights streamed through a shared-memory ring by
+// 1-D bulk copies (gemv_tma_kernel; tensor-core math only).
+cudaError_t launch_gemv_tma(const GemvParams& p, int planes, int wbytes, size_t smem, bool pdl,
+                            cudaStream_t stream);
 
 // The decode-MLP stack in one cooperative launch.  Per layer l: phase 1 =
 // gu (RMSNorm(h) -> gate||up -> SiLU*up -> act), phase 2 = dn (act -> down ->
@@ -162,6 +175,10 @@ struct StackParams {
 cudaError_t launch_stack(const StackParams& sp, int grid, int wbytes, size_t smem, cudaStream_t stream);
 // Largest grid of stack_kernel<wbytes> that can be co-resident with `smem` bytes per CTA.
 cudaError_t stack_max_coresident(int wbytes, size_t smem, int num_sms, int* max_grid);
+// The stack on the TMA pipeline (gu and dn carry the same ring: off_ring,
+// n_stages, stage_bytes), and its co-residency limit.
+cudaError_t launch_stack_tma(const StackParams& sp, int grid, int wbytes, size_t smem, cudaStream_t stream);
+cudaError_t stack_tma_max_coresident(int wbytes, size_t smem, int num_sms, int* max_grid);
 // Raises the dynamic shared-memory limit of every kernel variant.
 cudaError_t gemv_set_smem_limit(int bytes);
 
