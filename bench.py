@@ -584,7 +584,10 @@ def run_ours(args):
     tf = ROOT / "profiles" / "traffic.json"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(f"gate_up_m{M}_tp{tp}")
-    roofline = {"kernel": "gemv_streamk_kernel<2,1,0,1> (RMSNorm + gate||up + SiLU*up)",
+    gu_plan = gu_op.plan(M)
+    gu_kernel = ("gemv_tma_kernel<2,1,{}>".format(1 if tp > 1 and tps.fused else 0)
+                 if gu_plan["pipe"] == b2g.PIPE_TMA else "gemv_streamk_kernel<2,1,0,1>")
+    roofline = {"kernel": f"{gu_kernel} (RMSNorm + gate||up + SiLU*up)",
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "traffic": traffic,
                 "peak_source": f"{peak_kind} hbm_gbs (STREAM-style copy)",

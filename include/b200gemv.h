@@ -148,8 +148,9 @@ b2g_status b2g_destroy(b2g_op* op);
  *    warp streams the CTA's range into a shared-memory ring of 16 KB stages
  *    with 1-D bulk copies, 16 warps compute from it (tensor-core math only;
  *    ops whose x rows leave fewer than two stages of shared memory stay on
- *    REGISTERS).  AUTO (default) picks per shape.  The packed layout is the
- *    same for both. */
+ *    REGISTERS).  AUTO (default): TMA for two-plane (gate||up) ops,
+ *    REGISTERS otherwise (the faster pair per decode layer on B200).  The
+ *    packed layout is the same for both. */
 enum { B2G_OPT_MATH = 1, B2G_OPT_GRID = 2, B2G_OPT_PARTITION = 3, B2G_OPT_KSPLIT = 4, B2G_OPT_PIPE = 5 };
 enum { B2G_PARTITION_AUTO = 0, B2G_PARTITION_UNITS = 1, B2G_PARTITION_TILES = 2 };
 enum { B2G_PIPE_AUTO = 0, B2G_PIPE_REGISTERS = 1, B2G_PIPE_TMA = 2 };
@@ -266,9 +267,10 @@ b2g_status b2g_enqueue_static(const b2g_op* op, const b2g_enqueue_args* args, b2
  * layers alternate between the inbox's two buffers (`buf`).  A wait that
  * expires sets the device error word (B2G_ERR_PEER_TIMEOUT class, code 4);
  * while the word is set, later waits give up at once (a lost peer costs one
- * 2 s wait, not one per layer).  b2g_tp_gather then leaves h as it was; a
- * GATHER launch still runs its GEMV on whatever its inbox holds.  Either way
- * every row produced since the error is invalid: read and clear the word
+ * 2 s wait, not one per layer).  b2g_tp_gather then leaves h as it was, and
+ * a GATHER launch writes neither h_out nor its own output rows (its tiles'
+ * split-K handshakes still complete, so the workspace stays consistent).
+ * Every row produced since the error is invalid: read and clear the word
  * (b2g_device_error), then re-zero the exchange buffers and the ops'
  * workspaces (b2g_workspace_init) before the next step.
  * ------------------------------------------------------------------------ */

@@ -161,9 +161,14 @@ bool plan_launch(const b2g_op* op, int m, LaunchPlan* lp) {
   return lp->smem <= (size_t)op->smem_optin;
 }
 
-// Whether calls with m rows run on the TMA pipeline.
+// Whether calls with m rows run on the TMA pipeline.  AUTO takes it for
+// two-plane (gate||up) ops: measured per decode layer on B200 (28 layers,
+// per-layer launches), gate||up on TMA and down on registers 22.6-23.0 us
+// at M = 8 and 21.3-21.7 at M = 1, against 23.8 / 22.7 with both on
+// registers and 24.0-25.5 / 20.7-22.5 with both on TMA.
 bool use_tma(const b2g_op* op, const LaunchPlan& lp) {
   if (op->math != kMathMma || lp.n_stages < 2) return false;
+  if (op->pipe == B2G_PIPE_AUTO) return op->planes == 2;
   return op->pipe == B2G_PIPE_TMA;
 }
 

@@ -205,7 +205,8 @@ __device__ __forceinline__ float rms_of(const GemvParams& p, const float* red, i
 // into those kernels).
 template <int P, bool TPX>
 __device__ __forceinline__ void epilogue(const GemvParams& p, const Io& io, int j, int tile, const float (&v)[P][4],
-                                         int lane, const float* red, const Epi& e, __half* stage) {
+                                         int lane, const float* red, const Epi& e, __half* stage, bool write) {
+  if (!write) return;  // a tensor-parallel gather whose wait expired: rows void, nothing written
   const int g = lane >> 2, q = lane & 3;
   // this lane's two token rows, 2q and 2q + 1
   const float r0 = (red && 2 * q < p.M) ? rms_of(p, red, 2 * q) : 1.0f;
@@ -251,7 +252,8 @@ __device__ __forceinline__ void epilogue(const GemvParams& p, const Io& io, int 
 // contributing CTA sum all partials in (k-range, CTA) order.
 template <int P, bool TPX>
 __device__ __forceinline__ void finish_vt(const GemvParams& p, const Io& io, int vt, int j, const float (&v)[P][4],
-                                          int lane, const float* red, const Epi& e, __half* stage) {
+                                          int lane, const float* red, const Epi& e, __half* stage,
+                                          bool write = true) {
   const int ks = fdiv(vt, p.div_tiles);
   const int tile = vt - ks * p.n_tiles;
   // Contributors of k-range k: CTAs cta_of(a_k) .. cta_of(a_k + kbpv - 1).
@@ -315,7 +317,7 @@ __device__ __forceinline__ void finish_vt(const GemvParams& p, const Io& io, int
     }
     if (lane == 0) p.counters[tile] = 0;
   }
-  epilogue<P, TPX>(p, io, j, tile, s, lane, red, e, stage);
+  epilogue<P, TPX>(p, io, j, tile, s, lane, red, e, stage, write);
 }
 
 // Sum of squares of 8 halves, in one fixed order (stage_x and gather_x share
@@ -463,6 +465,7 @@ __device__ void gather_x(const GemvParams& p, __half* xs, int krange, int tid, f
   const int M = p.M;
   if (tid == 0) *verdict = tp_wait_arrivals(p.tp, p.error) ? 1 : 0;
   sync();
+  const bool ok = *verdict != 0;  // false: the wait expired; h_out is left as it was
   const int nch = krange / 8;
   constexpr int B = 4;
   float ss[8];
@@ -496,7 +499,7 @@ __device__ void gather_x(const GemvParams& p, __half* xs, int krange, int tid, f
           if (m < M) {
             const uint4 v = round8(a[b]);
             sts128(xs + (size_t)m * p.x_rs + c * 8, v);
-            if (c % p.grid == (int)blockIdx.x)
+            if (ok && c % p.grid == (int)blockIdx.x)
               *reinterpret_cast<uint4*>(p.tp.h_out + (size_t)m * p.tp.ldh + c * 8) = v;
             if (red) ss[m] += sumsq8(v);
           }
@@ -828,6 +831,9 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
   // ---- combine: the warps' partials in warp order, then finish each tile
   __syncthreads();
   const int nvt = vt_last - vt_first + 1;
+  // A tensor-parallel gather whose wait expired: the tiles' handshakes still
+  // run, their rows are not written.
+  const bool write = !(gather && *reinterpret_cast<volatile int*>(smem + kOffMisc) == 0);
   for (int j = warp; j < nvt; j += W) {
     float v[P][4];
 #pragma unroll
@@ -846,7 +852,7 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
     // slot j's shared memory is this warp's alone once summed: the PUSH stage
     __syncwarp();
     finish_vt<P, TP>(p, io, vt_first + j, j, v, lane, p.rmsnorm ? red : nullptr, epi,
-                 reinterpret_cast<__half*>(slots + (size_t)j * W * P * 32));
+                 reinterpret_cast<__half*>(slots + (size_t)j * W * P * 32), write);
   }
 #ifdef B2G_TRACE
   __syncthreads();
@@ -1133,6 +1139,9 @@ __device__ void tma_stream(const GemvParams& p, const Io& io, uint8_t* smem, con
 
   // ---- combine the warps' partials in warp order, then finish each tile
   consumer_sync();
+  // A tensor-parallel gather whose wait expired: the tiles' handshakes still
+  // run, their rows are not written.
+  const bool write = !(TPX && p.tp.mode == kTpGather && *reinterpret_cast<volatile int*>(smem + kOffMisc) == 0);
   for (int jj = warp; jj < nvt; jj += W) {
     float v[P][4];
 #pragma unroll
@@ -1150,7 +1159,7 @@ __device__ void tma_stream(const GemvParams& p, const Io& io, uint8_t* smem, con
     }
     __syncwarp();
     finish_vt<P, TPX>(p, io, vt_first + jj, jj, v, lane, p.rmsnorm ? red : nullptr, epi,
-                      reinterpret_cast<__half*>(slots + (size_t)jj * W * P * 32));
+                      reinterpret_cast<__half*>(slots + (size_t)jj * W * P * 32), write);
   }
   if (tid == 0) STRACE(trace_base + 3);
 }

@@ -95,6 +95,42 @@ def test_gather_wait_expires(b2g, orc, syn, cuda):
     st.close_comm()
 
 
+@pytest.mark.parametrize("pipe", ["registers", "tma"])
+def test_gather_gemv_wait_expires_writes_nothing(b2g, orc, syn, cuda, pipe):
+    """A gate||up launch in GATHER mode whose wait for the peers' arrivals
+    expires records the peer-wait code and writes neither h (the all-reduced
+    rows) nor its own output rows."""
+    tp = _tp(b2g)
+    H, I = 256, 512
+    st = tp.TPStack(H, I, 1, rank=0, world=1, max_m=8, fused=True)
+    code = {"registers": b2g.PIPE_REGISTERS, "tma": b2g.PIPE_TMA}[pipe]
+    st.gate_up.set_option(b2g.OPT_PIPE, code)
+    assert st.gate_up.plan(2)["pipe"] == code
+    comm = st.setup_comm(cuda)
+    wg, wu = (b2g.quantize_e4m3(torch.from_numpy(syn.weights(s, H, I)).to(cuda), "channel_fp32") for s in (81, 82))
+    pgu = st.gate_up.prepack(wg[0], wu[0])
+    sgu = torch.cat([wg[1], wu[1]])
+    _, _, epoch = b2g.tp_comm_layout(st._comm_buf.data_ptr(), 1, 8, H)
+    off = epoch - st._comm_buf.data_ptr()
+    st._comm_buf[off:off + 4].view(torch.int32).fill_(1)  # one round expected, none pushed
+    h = torch.full((2, H), 3.0, dtype=torch.float16, device=cuda)
+    act = torch.full((2, I), 5.0, dtype=torch.float16, device=cuda)
+    ws = st.workspace(cuda)
+    st.gate_up.enqueue_tp(comm, b2g.TP_GATHER, 0, h, pgu, sgu, y=act, workspace=ws, push_op=st.down, h_out=h)
+    torch.cuda.synchronize()
+    assert b2g.device_error(clear=True) == 4  # peer wait expired
+    assert bool((h == 3.0).all()) and bool((act == 5.0).all())
+    # the workspace's tile counters are back at zero: the op runs normally afterwards
+    st._comm_buf.zero_()
+    y = st.gate_up.enqueue(h, pgu, sgu, workspace=ws)
+    torch.cuda.synchronize()
+    want = orc.gate_up_silu(orc.rmsnorm(h.cpu().numpy()), wg[0].cpu().numpy(), wu[0].cpu().numpy(),
+                            orc.WTYPE_FP8, orc.SCALE_CHANNEL_FP32, wg[1].cpu().numpy(), wu[1].cpu().numpy())
+    assert orc.compare(y.cpu().numpy(), want.astype(np.float64))["rel_l2"] <= 5e-3
+    assert b2g.device_error() == 0
+    st.close_comm()
+
+
 # --------------------------------------------------------------------------
 # Two ranks, one GPU each
 # --------------------------------------------------------------------------
