@@ -703,7 +703,9 @@ struct NoHook {
   __device__ __forceinline__ void operator()(T&) const {}
 };
 
-template <int P, int WB, int MATH, int R, class AfterStream, bool TP>
+// SCALES_LOADED: the caller loaded the tiles' scales already (before the
+// dependency wait); the phase loads only the residual rows.
+template <int P, int WB, int MATH, int R, class AfterStream, bool TP, bool SCALES_LOADED = false>
 __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uint8_t* smem,
                                           uint4 (&ring)[R], uint64_t pol, AfterStream after_stream,
                                           int trace_base = -1) {
@@ -737,7 +739,10 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
   }
   if (active) {
     if (!gather) stage_x(p, io, xs, k_lo, krange, tid, p.rmsnorm ? red : nullptr);
-    load_epi<P>(p, io, epi, vt_first, vt_last - vt_first + 1, tid);
+    if (SCALES_LOADED)
+      load_residual<P>(p, io, epi, vt_first, vt_last - vt_first + 1, tid);
+    else
+      load_epi<P>(p, io, epi, vt_first, vt_last - vt_first + 1, tid);
   }
   for (int i = tid; i < p.n_slots * W * P * 32; i += NT) slots[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   __syncthreads();
@@ -892,10 +897,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_
     }
   }
   pdl_launch_dependents();
+  // The scales are constants: into shared memory before the wait, off the
+  // critical path (an HBM round trip after it otherwise).
+  if ((int)blockIdx.x < p.grid) {
+    const int u0 = range_start(p, blockIdx.x), u1 = range_start(p, blockIdx.x + 1);
+    if (u1 > u0) {
+      const int vt_first = fdiv(u0, p.div_kbpv);
+      load_scales<P>(p, io_of_params(p), epi_of(p, smem, P), vt_first, fdiv(u1 - 1, p.div_kbpv) - vt_first + 1, tid);
+    }
+  }
   pdl_wait();
   if (tid == 0) TRACE(1);
   if (TPX && p.tp.mode == kTpPush && blockIdx.x == 0 && tid == 0) atomicAdd(p.tp.epoch, 1u);
-  run_phase<P, WB, MATH, R, NoHook, TPX>(p, io_of_params(p), smem, ring, pol, NoHook{});
+  run_phase<P, WB, MATH, R, NoHook, TPX, true>(p, io_of_params(p), smem, ring, pol, NoHook{});
   if (TPX && p.tp.mode == kTpPush) {
     // This CTA's peer stores are done: one arrival on every rank.
     __syncthreads();
