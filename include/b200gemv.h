@@ -148,9 +148,8 @@ b2g_status b2g_destroy(b2g_op* op);
  *    warp streams the CTA's range into a shared-memory ring of 16 KB stages
  *    with 1-D bulk copies, 16 warps compute from it (tensor-core math only;
  *    ops whose x rows leave fewer than two stages of shared memory stay on
- *    REGISTERS).  AUTO (default): TMA for two-plane (gate||up) ops,
- *    REGISTERS otherwise (the faster pair per decode layer on B200).  The
- *    packed layout is the same for both. */
+ *    REGISTERS).  AUTO (default) = REGISTERS, the faster of the two per
+ *    decode layer on B200.  The packed layout is the same for both. */
 enum { B2G_OPT_MATH = 1, B2G_OPT_GRID = 2, B2G_OPT_PARTITION = 3, B2G_OPT_KSPLIT = 4, B2G_OPT_PIPE = 5 };
 enum { B2G_PARTITION_AUTO = 0, B2G_PARTITION_UNITS = 1, B2G_PARTITION_TILES = 2 };
 enum { B2G_PIPE_AUTO = 0, B2G_PIPE_REGISTERS = 1, B2G_PIPE_TMA = 2 };

@@ -161,14 +161,13 @@ bool plan_launch(const b2g_op* op, int m, LaunchPlan* lp) {
   return lp->smem <= (size_t)op->smem_optin;
 }
 
-// Whether calls with m rows run on the TMA pipeline.  AUTO takes it for
-// two-plane (gate||up) ops: measured per decode layer on B200 (28 layers,
-// per-layer launches), gate||up on TMA and down on registers 22.6-23.0 us
-// at M = 8 and 21.3-21.7 at M = 1, against 23.8 / 22.7 with both on
-// registers and 24.0-25.5 / 20.7-22.5 with both on TMA.
+// Whether calls with m rows run on the TMA pipeline.  AUTO keeps the
+// register pipeline: measured per decode layer on B200 (28 layers,
+// per-layer launches, both kernels loading their scales before the
+// dependency wait), both ops on registers 22.9 us at M = 8 and 22.1 at
+// M = 1; gate||up on TMA 23.2-23.3 / 22.0-22.2; both on TMA 25.0 / 21.5.
 bool use_tma(const b2g_op* op, const LaunchPlan& lp) {
   if (op->math != kMathMma || lp.n_stages < 2) return false;
-  if (op->pipe == B2G_PIPE_AUTO) return op->planes == 2;
   return op->pipe == B2G_PIPE_TMA;
 }
 
