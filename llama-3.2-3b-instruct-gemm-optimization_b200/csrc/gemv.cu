@@ -927,7 +927,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_
 // ---------------------------------------------------------------------------
 // Warp 16 (lane 0, the producer) streams a CTA's contiguous range of the
 // packed weights into a ring of n_stages stages with 1-D bulk copies
-// (cp.async.bulk from this GPU's memory; no multicast).  Warps 0..15 (the
+// (cp.async.bulk, one CTA's own copies from this GPU's memory).  Warps 0..15 (the
 // consumers) take the units as the register-ring kernel does (warp w: units
 // w, w + 16, ... of the range) and read each lane's 16-byte A fragment from
 // the ring.  Stage s of the ring's life fills slot s % n_stages; full[slot]
