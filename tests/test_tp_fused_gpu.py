@@ -137,7 +137,7 @@ def test_gather_gemv_wait_expires_writes_nothing(b2g, orc, syn, cuda, pipe):
 HID, INT, NL, MM = 3072, 8192, 2, 8
 
 
-def _rank(rank, world, port, out):
+def _rank(rank, world, port, out, nl=NL, steps=1):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
@@ -145,18 +145,22 @@ def _rank(rank, world, port, out):
     dist.init_process_group("gloo", rank=rank, world_size=world)  # handle exchange only
     b2g, orc, syn = load_b2g(), load_oracle(), load_synthetic()
     tp = __import__("b2g.tp", fromlist=["TPStack"])
-    layers = _weights(orc, syn, HID, INT, NL, 4000)
-    st = tp.TPStack(HID, INT, NL, rank=rank, world=world, max_m=8, fused=True)
+    layers = _weights(orc, syn, HID, INT, nl, 4000)
+    st = tp.TPStack(HID, INT, nl, rank=rank, world=world, max_m=8, fused=True)
     _load_layers(st, layers, dev)
     st.setup_comm(dev)
     h = torch.from_numpy(syn.hidden_state(MM, HID)).to(dev)
     act = torch.empty(MM, st.shard, dtype=torch.float16, device=dev)
-    st.enqueue(h, act, st.workspace(dev))
+    ws = st.workspace(dev)
+    outs = []
+    for _ in range(steps):  # consecutive steps: inbox buffers, counters and epochs carry over
+        st.enqueue(h, act, ws)
+        outs.append(h.cpu().numpy())
     torch.cuda.synchronize()
     err = b2g.device_error()
     dist.barrier()
     st.close_comm()
-    np.save(out + f".{rank}.npy", h.cpu().numpy())
+    np.save(out + f".{rank}.npy", np.stack(outs))
     with open(out + f".{rank}.err", "w") as f:
         f.write(str(err))
     dist.barrier()
@@ -169,22 +173,27 @@ def _port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("which", ["two", "all"])
-def test_fused_ranks(b2g, orc, syn, cuda, tmp_path, which):
+@pytest.mark.parametrize("which,nl,steps", [("two", NL, 1), ("two", 2, 2), ("two", 3, 2), ("all", NL, 1)])
+def test_fused_ranks(b2g, orc, syn, cuda, tmp_path, which, nl, steps):
+    """Every rank's rows bitwise equal and, on rank 0, the oracle's sharded
+    stack, after each of `steps` consecutive steps (an odd layer count makes
+    the second step start on the other inbox buffer)."""
     n = min(torch.cuda.device_count(), 8)
     if n < 2 or (which == "all" and n == 2):
         pytest.skip("needs two GPUs" if n < 2 else "all = two here")
     world = 2 if which == "two" else n
     import torch.multiprocessing as mp
     out = str(tmp_path / "h")
-    mp.spawn(_rank, args=(world, _port(), out), nprocs=world, join=True)
+    mp.spawn(_rank, args=(world, _port(), out, nl, steps), nprocs=world, join=True)
     got = [np.load(out + f".{r}.npy") for r in range(world)]
     assert [open(out + f".{r}.err").read() for r in range(world)] == ["0"] * world
     for r in range(1, world):
         assert np.array_equal(got[r], got[0]), r  # the same sum, in the same order, on every rank
-    layers = _weights(orc, syn, HID, INT, NL, 4000)
+    layers = _weights(orc, syn, HID, INT, nl, 4000)
     want = syn.hidden_state(MM, HID)
-    for L in layers:
-        want = orc.mlp_layer_tp(want, L, world)
-    r = orc.compare(got[0], want.astype(np.float64))
-    assert r["rel_l2"] <= 5e-3, r
+    for step in range(steps):
+        for L in layers:
+            want = orc.mlp_layer_tp(want, L, world)
+        r = orc.compare(got[0][step], want.astype(np.float64))
+        assert r["rel_l2"] <= 5e-3 * (step + 1), (step, r)
+        want = got[0][step]  # the next step starts from the rows the GPU produced
