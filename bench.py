@@ -453,6 +453,11 @@ def run_ours(args):
         tps = importlib.import_module("b2g.tp").TPStack(HIDDEN, INTER, LAYERS, rank=rank, world=world, max_m=M,
                                                         fused=args.tp_mode == "fused")
         gu_op, dn_op = tps.gate_up, tps.down
+    pipe = {"auto": b2g.PIPE_AUTO, "registers": b2g.PIPE_REGISTERS, "tma": b2g.PIPE_TMA}[args.pipe]
+    for op in (gu_op, dn_op):
+        op.set_option(b2g.OPT_PIPE, pipe)
+    if st is not None and args.stack_mode != "per_layer":
+        st.set_mode(args.stack_mode)
     want_ref = tp == 1 and not args.no_ref_kernels and REF_GPU_LIB.exists()
     layers = make_layers(b2g, torch, device, tp, rank, (gu_op, dn_op), M, keep_raw=want_ref)
     for i, L in enumerate(layers):
@@ -533,15 +538,22 @@ def run_ours(args):
     reps = max(5, args.steps // 20)
     detail_extra = {}
     if st is not None:
-        # The stack's other execution mode (one persistent cooperative launch
-        # per step), for comparison.
-        st.set_mode("persistent")
-        for _ in range(3):
-            step_stack()
-        ms_pl = timed(step_stack, reps) / reps
-        st.set_mode("per_layer")
-        detail_extra["persistent_kernel_ms_per_step"] = round(ms_pl, 5)
-        detail_extra["persistent_kernel_us_per_layer"] = round(ms_pl * 1e3 / LAYERS, 3)
+        # The stack's other execution modes (one persistent cooperative
+        # launch per step, on the register or the TMA pipeline), for
+        # comparison; recorded, not fatal.
+        for mode in ("persistent", "persistent_tma", "per_layer"):
+            if mode == args.stack_mode:
+                continue
+            try:
+                st.set_mode(mode)
+                for _ in range(3):
+                    step_stack()
+                ms_pl = timed(step_stack, reps) / reps
+                detail_extra[f"{mode}_ms_per_step"] = round(ms_pl, 5)
+                detail_extra[f"{mode}_us_per_layer"] = round(ms_pl * 1e3 / LAYERS, 3)
+            except Exception as e:
+                detail_extra[f"{mode}_error"] = f"{type(e).__name__}: {e}"
+        st.set_mode(args.stack_mode)
         # The same stack at every M of the metric's configs (one decode MLP
         # layer = fused gate||up + down, 28 distinct layers per step), each
         # replayed as a CUDA graph of one step; recorded, not fatal.
@@ -827,6 +839,10 @@ def main():
     ap.add_argument("--no-adjacent", action="store_true", help="skip timing qkv_proj / o_proj / lm_head")
     ap.add_argument("--tp-mode", choices=["fused", "nccl"], default="fused",
                     help="N > 1: all-reduce fused into the GEMVs over peer memory, or NCCL")
+    ap.add_argument("--pipe", choices=["auto", "registers", "tma"], default="auto",
+                    help="how the GEMV launches feed their weights (B2G_OPT_PIPE)")
+    ap.add_argument("--stack-mode", choices=["per_layer", "persistent", "persistent_tma"], default="per_layer",
+                    help="one GPU: the stack's execution mode for the timed step")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decode-MLP layers (28 = Llama-3.2-3B; fewer only for small profiling captures)")
     args = ap.parse_args()
