@@ -597,8 +597,9 @@ def run_ours(args):
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(f"gate_up_m{M}_tp{tp}")
     gu_plan = gu_op.plan(M)
-    gu_kernel = ("gemv_tma_kernel<2,1,{}>".format(1 if tp > 1 and tps.fused else 0)
-                 if gu_plan["pipe"] == b2g.PIPE_TMA else "gemv_streamk_kernel<2,1,0,1>")
+    exch = 1 if tp > 1 and tps.fused else 0
+    gu_kernel = (f"gemv_tma_kernel<2,1,{exch}>" if gu_plan["pipe"] == b2g.PIPE_TMA
+                 else f"gemv_streamk_kernel<2,1,0,{exch}>")
     roofline = {"kernel": f"{gu_kernel} (RMSNorm + gate||up + SiLU*up)",
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "traffic": traffic,

@@ -1431,19 +1431,13 @@ cudaError_t launch_variant(const GemvParams& p, size_t smem, bool pdl, cudaStrea
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if constexpr (P == 2) {
-    // The two-plane (gate||up) op always takes the instantiation with the
-    // exchange code, which then sits idle: measured chained on B200 at M = 8,
-    // 12.9 us per launch against 15.3 us for the one without it (24.9 against
-    // 25.3 us per decode layer; M = 1: 23.6 against 24.2).  The compiler
-    // schedules the common path differently in the two; the one-plane (down)
-    // op is the other way round (15.6 against 22.4 us cold under ncu), so it
-    // keeps the lean instantiation.
-    return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, true>, p);
-  } else {
-    if (p.tp.mode != kTpNone) return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, true>, p);
-    return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, false>, p);
-  }
+  // Only launches that exchange rows with other ranks take the instantiation
+  // with the tensor-parallel code (TPX): the lean one is smaller, and code
+  // size shows up as instruction-fetch stalls in every launch.  Measured on
+  // B200 per decode layer (28 layers, M = 8 / 1): gate||up on the lean
+  // instantiation 21.2 / 20.5 us, on the exchange-carrying one 22.9 / 22.1.
+  if (p.tp.mode != kTpNone) return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, true>, p);
+  return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, false>, p);
 }
 
 template <int P, int WB>
@@ -1576,6 +1570,10 @@ cudaError_t gemv_set_smem_limit(int bytes) {
   B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, false>))
   B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, true>))
   B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma, true>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma, false>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma, false>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma, false>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma, false>))
   B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, false>))
   B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, true>))
   B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma, true>))
