@@ -556,6 +556,9 @@ static b2g_status enqueue_impl(const b2g_op* op, const b2g_enqueue_args* a, cons
     p.pf_bytes = use_tma(op, lp) ? kPrefetchBytesTma : kPrefetchBytesPerCta;
   }
   if (tp) p.tp = *tp;
+  // One contributor per output tile (no K split, no tile shared between
+  // CTAs) and aligned rows: the lean kernel flavor.
+  p.lean = op->ksplit == 1 && op->max_contrib == 1 && aligned(a->x, 16) && a->ldx % 8 == 0 && op->K % 32 == 0;
   if (use_tma(op, lp)) {
     p.off_ring = lp.off_ring;
     p.n_stages = lp.n_stages;

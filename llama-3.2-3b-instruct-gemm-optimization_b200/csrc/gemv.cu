@@ -250,7 +250,9 @@ __device__ __forceinline__ void epilogue(const GemvParams& p, const Io& io, int 
 // A virtual tile's CTA-level sum is complete in v: finish it here if this CTA
 // is the tile's only contributor, else publish it and let the last
 // contributing CTA sum all partials in (k-range, CTA) order.
-template <int P, bool TPX>
+// SPLIT: the plan may share a virtual tile between CTAs (else every tile has
+// one contributor and the handshake code is not compiled in).
+template <int P, bool TPX, bool SPLIT = true>
 __device__ __forceinline__ void finish_vt(const GemvParams& p, const Io& io, int vt, int j, const float (&v)[P][4],
                                           int lane, const float* red, const Epi& e, __half* stage,
                                           bool write = true) {
@@ -262,9 +264,12 @@ __device__ __forceinline__ void finish_vt(const GemvParams& p, const Io& io, int
     const int a = (k * p.n_tiles + tile) * p.kbpv;
     return cta_of(p, a + p.kbpv - 1) - cta_of(p, a) + 1;
   };
-  int total = 0;
+  int total = 1;
+  if constexpr (SPLIT) {
+    total = 0;
 #pragma unroll 1
-  for (int k = 0; k < p.ksplit; ++k) total += count_of(k);
+    for (int k = 0; k < p.ksplit; ++k) total += count_of(k);
+  }
   float s[P][4];
 #pragma unroll
   for (int pl = 0; pl < P; ++pl)
@@ -355,11 +360,15 @@ __device__ __forceinline__ void reduce_rows(float (&ss)[8], int tid, float* red)
 // give each row's sum of squares: every thread sums its own chunks, each warp
 // reduces across its lanes and writes red[warp * 8 + m]; rms_of() adds the
 // warps in order (deterministic).
+// VEC_ONLY: the host has checked that every row piece is 16-byte aligned and
+// inside K (the element path is then not compiled in).
+template <bool VEC_ONLY = false>
 __device__ void stage_x(const GemvParams& p, const Io& io, __half* xs, int k_lo, int krange, int tid,
                         float* red) {
   const int M = p.M, K = p.K;
   const int nch = krange / 8;
-  const bool vec = ((reinterpret_cast<uintptr_t>(io.x) & 15) == 0) && ((io.ldx & 7) == 0) && k_lo + krange <= K;
+  const bool vec =
+      VEC_ONLY || (((reinterpret_cast<uintptr_t>(io.x) & 15) == 0) && ((io.ldx & 7) == 0) && k_lo + krange <= K);
   float ss[8];
 #pragma unroll
   for (int m = 0; m < 8; ++m) ss[m] = 0.f;
@@ -705,7 +714,9 @@ struct NoHook {
 
 // SCALES_LOADED: the caller loaded the tiles' scales already (before the
 // dependency wait); the phase loads only the residual rows.
-template <int P, int WB, int MATH, int R, class AfterStream, bool TP, bool SCALES_LOADED = false>
+// LEAN: whole virtual tiles per CTA and aligned activation rows (the
+// host-checked common case: no split-tile handshake, vector staging only).
+template <int P, int WB, int MATH, int R, class AfterStream, bool TP, bool SCALES_LOADED = false, bool LEAN = false>
 __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uint8_t* smem,
                                           uint4 (&ring)[R], uint64_t pol, AfterStream after_stream,
                                           int trace_base = -1) {
@@ -738,7 +749,7 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
              reinterpret_cast<volatile int*>(smem + kOffMisc), [] { __syncthreads(); });
   }
   if (active) {
-    if (!gather) stage_x(p, io, xs, k_lo, krange, tid, p.rmsnorm ? red : nullptr);
+    if (!gather) stage_x<LEAN>(p, io, xs, k_lo, krange, tid, p.rmsnorm ? red : nullptr);
     if (SCALES_LOADED)
       load_residual<P>(p, io, epi, vt_first, vt_last - vt_first + 1, tid);
     else
@@ -856,7 +867,7 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
     }
     // slot j's shared memory is this warp's alone once summed: the PUSH stage
     __syncwarp();
-    finish_vt<P, TP>(p, io, vt_first + j, j, v, lane, p.rmsnorm ? red : nullptr, epi,
+    finish_vt<P, TP, !LEAN>(p, io, vt_first + j, j, v, lane, p.rmsnorm ? red : nullptr, epi,
                  reinterpret_cast<__half*>(slots + (size_t)j * W * P * 32), write);
   }
 #ifdef B2G_TRACE
@@ -868,8 +879,17 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
 // ---------------------------------------------------------------------------
 // One GEMV per launch
 // ---------------------------------------------------------------------------
-template <int P, int WB, int MATH, bool TPX>
+// FLAVOR: kFlavorLean (whole tiles, aligned rows, no exchange),
+// kFlavorGeneral (any plan and rows, no exchange) or kFlavorExchange (the
+// tensor-parallel PUSH / GATHER code compiled in).  Code size shows up as
+// instruction-fetch stalls in every launch, so each launch takes the
+// smallest flavor that covers it.
+enum : int { kFlavorLean = 0, kFlavorGeneral = 1, kFlavorExchange = 2 };
+
+template <int P, int WB, int MATH, int FLAVOR>
 __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_constant__ GemvParams p) {
+  constexpr bool TPX = FLAVOR == kFlavorExchange;
+  constexpr bool LEAN = FLAVOR == kFlavorLean;
   extern __shared__ __align__(1024) uint8_t smem[];
   // 128 KB of weights in flight per SM (16 B x 512 threads x 16); the FFMA
   // variant needs the registers for its accumulators and keeps half.
@@ -909,7 +929,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_
   pdl_wait();
   if (tid == 0) TRACE(1);
   if (TPX && p.tp.mode == kTpPush && blockIdx.x == 0 && tid == 0) atomicAdd(p.tp.epoch, 1u);
-  run_phase<P, WB, MATH, R, NoHook, TPX, true>(p, io_of_params(p), smem, ring, pol, NoHook{});
+  run_phase<P, WB, MATH, R, NoHook, TPX, true, LEAN>(p, io_of_params(p), smem, ring, pol, NoHook{});
   if (TPX && p.tp.mode == kTpPush) {
     // This CTA's peer stores are done: one arrival on every rank.
     __syncthreads();
@@ -1431,13 +1451,13 @@ cudaError_t launch_variant(const GemvParams& p, size_t smem, bool pdl, cudaStrea
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  // Only launches that exchange rows with other ranks take the instantiation
-  // with the tensor-parallel code (TPX): the lean one is smaller, and code
-  // size shows up as instruction-fetch stalls in every launch.  Measured on
-  // B200 per decode layer (28 layers, M = 8 / 1): gate||up on the lean
-  // instantiation 21.2 / 20.5 us, on the exchange-carrying one 22.9 / 22.1.
-  if (p.tp.mode != kTpNone) return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, true>, p);
-  return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, false>, p);
+  // The smallest flavor that covers the launch.  Measured on B200 per decode
+  // layer (28 layers, M = 8 / 1): gate||up on the exchange flavor 22.9 /
+  // 22.1 us, on the general one 21.2 / 20.5, both ops on the lean one
+  // 20.6 / 19.6.
+  if (p.tp.mode != kTpNone) return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, kFlavorExchange>, p);
+  if (p.lean) return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, kFlavorLean>, p);
+  return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, kFlavorGeneral>, p);
 }
 
 template <int P, int WB>
@@ -1567,22 +1587,30 @@ cudaError_t gemv_set_smem_limit(int bytes) {
   cudaError_t e = cudaSuccess, r;
 #define B2G_LIM(K) \
   if ((r = cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes)) != cudaSuccess) e = r;
-  B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, false>))
-  B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, true>))
-  B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma, true>))
-  B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma, false>))
-  B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma, false>))
-  B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma, false>))
-  B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma, false>))
-  B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, false>))
-  B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, true>))
-  B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma, true>))
-  B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, false>))
-  B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, true>))
-  B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma, true>))
-  B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma, false>))
-  B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma, true>))
-  B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma, true>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, kFlavorLean>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, kFlavorGeneral>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, kFlavorLean>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, kFlavorGeneral>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, kFlavorLean>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, kFlavorGeneral>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma, kFlavorLean>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma, kFlavorGeneral>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma, kFlavorLean>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma, kFlavorGeneral>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma, kFlavorLean>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma, kFlavorGeneral>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma, kFlavorLean>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma, kFlavorGeneral>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma, kFlavorLean>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma, kFlavorGeneral>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma, kFlavorExchange>))
   B2G_LIM((stack_kernel<1>))
   B2G_LIM((stack_kernel<2>))
   B2G_LIM((gemv_tma_kernel<1, 1, false>))

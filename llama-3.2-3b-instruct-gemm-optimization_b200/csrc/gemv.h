@@ -121,6 +121,8 @@ struct GemvParams {
   int off_epi;    // shared-memory byte offset of the epilogue inputs
   int off_x;      // shared-memory byte offset of the x rows
   int x_rs;       // x row stride in shared memory (halves)
+  int lean;       // one contributor per output tile (ksplit 1, max_contrib 1) and every
+                  // x row piece 16-byte aligned and inside K: the lean kernel flavor applies
   int off_ring;   // TMA pipeline: shared-memory byte offset of the weight ring
   int n_stages;   // ring stages (<= kMaxStages)
   int stage_bytes;
