@@ -716,7 +716,9 @@ struct NoHook {
 // dependency wait); the phase loads only the residual rows.
 // LEAN: whole virtual tiles per CTA and aligned activation rows (the
 // host-checked common case: no split-tile handshake, vector staging only).
-template <int P, int WB, int MATH, int R, class AfterStream, bool TP, bool SCALES_LOADED = false, bool LEAN = false>
+// TP: the PUSH epilogue is compiled in; GATHERX: the GATHER staging is.
+template <int P, int WB, int MATH, int R, class AfterStream, bool TP, bool SCALES_LOADED = false, bool LEAN = false,
+          bool GATHERX = TP>
 __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uint8_t* smem,
                                           uint4 (&ring)[R], uint64_t pol, AfterStream after_stream,
                                           int trace_base = -1) {
@@ -742,7 +744,7 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
 
   // ---- activations
   if (tid == 0) STRACE(trace_base);
-  const bool gather = TP && p.tp.mode == kTpGather;
+  const bool gather = GATHERX && p.tp.mode == kTpGather;
   if (gather) {
     // every CTA takes part (the wait and the write-back of the reduced rows)
     gather_x(p, xs, active ? krange : p.K / 8 * 8, tid, p.rmsnorm ? red : nullptr,
@@ -880,15 +882,16 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
 // One GEMV per launch
 // ---------------------------------------------------------------------------
 // FLAVOR: kFlavorLean (whole tiles, aligned rows, no exchange),
-// kFlavorGeneral (any plan and rows, no exchange) or kFlavorExchange (the
-// tensor-parallel PUSH / GATHER code compiled in).  Code size shows up as
-// instruction-fetch stalls in every launch, so each launch takes the
-// smallest flavor that covers it.
-enum : int { kFlavorLean = 0, kFlavorGeneral = 1, kFlavorExchange = 2 };
+// kFlavorGeneral (any plan and rows, no exchange), kFlavorPush (the
+// tensor-parallel PUSH epilogue compiled in) or kFlavorGather (the GATHER
+// staging compiled in).  Code size shows up as instruction-fetch stalls in
+// every launch, so each launch takes the smallest flavor that covers it.
+enum : int { kFlavorLean = 0, kFlavorGeneral = 1, kFlavorPush = 2, kFlavorGather = 3 };
 
 template <int P, int WB, int MATH, int FLAVOR>
 __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_constant__ GemvParams p) {
-  constexpr bool TPX = FLAVOR == kFlavorExchange;
+  constexpr bool TPX = FLAVOR == kFlavorPush;  // the PUSH epilogue and arrivals
+  constexpr bool GATHERX = FLAVOR == kFlavorGather;
   constexpr bool LEAN = FLAVOR == kFlavorLean;
   extern __shared__ __align__(1024) uint8_t smem[];
   // 128 KB of weights in flight per SM (16 B x 512 threads x 16); the FFMA
@@ -929,7 +932,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_
   pdl_wait();
   if (tid == 0) TRACE(1);
   if (TPX && p.tp.mode == kTpPush && blockIdx.x == 0 && tid == 0) atomicAdd(p.tp.epoch, 1u);
-  run_phase<P, WB, MATH, R, NoHook, TPX, true, LEAN>(p, io_of_params(p), smem, ring, pol, NoHook{});
+  run_phase<P, WB, MATH, R, NoHook, TPX, true, LEAN, GATHERX>(p, io_of_params(p), smem, ring, pol, NoHook{});
   if (TPX && p.tp.mode == kTpPush) {
     // This CTA's peer stores are done: one arrival on every rank.
     __syncthreads();
@@ -1455,7 +1458,8 @@ cudaError_t launch_variant(const GemvParams& p, size_t smem, bool pdl, cudaStrea
   // layer (28 layers, M = 8 / 1): gate||up on the exchange flavor 22.9 /
   // 22.1 us, on the general one 21.2 / 20.5, both ops on the lean one
   // 20.6 / 19.6.
-  if (p.tp.mode != kTpNone) return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, kFlavorExchange>, p);
+  if (p.tp.mode == kTpPush) return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, kFlavorPush>, p);
+  if (p.tp.mode == kTpGather) return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, kFlavorGather>, p);
   if (p.lean) return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, kFlavorLean>, p);
   return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, kFlavorGeneral>, p);
 }
@@ -1589,28 +1593,36 @@ cudaError_t gemv_set_smem_limit(int bytes) {
   if ((r = cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes)) != cudaSuccess) e = r;
   B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, kFlavorLean>))
   B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, kFlavorGeneral>))
-  B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, kFlavorPush>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, kFlavorGather>))
   B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, kFlavorLean>))
   B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, kFlavorGeneral>))
-  B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, kFlavorPush>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, kFlavorGather>))
   B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, kFlavorLean>))
   B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, kFlavorGeneral>))
-  B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, kFlavorPush>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, kFlavorGather>))
   B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma, kFlavorLean>))
   B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma, kFlavorGeneral>))
-  B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma, kFlavorPush>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma, kFlavorGather>))
   B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma, kFlavorLean>))
   B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma, kFlavorGeneral>))
-  B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma, kFlavorPush>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathMma, kFlavorGather>))
   B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma, kFlavorLean>))
   B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma, kFlavorGeneral>))
-  B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma, kFlavorPush>))
+  B2G_LIM((gemv_streamk_kernel<2, 1, kMathFfma, kFlavorGather>))
   B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma, kFlavorLean>))
   B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma, kFlavorGeneral>))
-  B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma, kFlavorPush>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathMma, kFlavorGather>))
   B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma, kFlavorLean>))
   B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma, kFlavorGeneral>))
-  B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma, kFlavorExchange>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma, kFlavorPush>))
+  B2G_LIM((gemv_streamk_kernel<2, 2, kMathFfma, kFlavorGather>))
   B2G_LIM((stack_kernel<1>))
   B2G_LIM((stack_kernel<2>))
   B2G_LIM((gemv_tma_kernel<1, 1, false>))
