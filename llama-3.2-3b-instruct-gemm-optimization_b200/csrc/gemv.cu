@@ -1560,6 +1560,9 @@ cudaError_t stack_max_coresident(int wbytes, size_t smem, int num_sms, int* max_
 namespace {
 __global__ void __launch_bounds__(256) tp_gather_kernel(const __grid_constant__ TpParams tp, int m_rows, int* err) {
   __shared__ int verdict;
+  // A launch chained after this one (programmatic dependent launch) may start
+  // its weight stream now; it reads h only after its own dependency wait.
+  pdl_launch_dependents();
   if (threadIdx.x == 0) verdict = tp_wait_arrivals(tp, err) ? 1 : 0;
   __syncthreads();
   if (!verdict) return;  // reported through the error word; h is left as it was

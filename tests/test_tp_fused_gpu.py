@@ -43,12 +43,16 @@ def _load_layers(st, layers, dev):
         st.prepack_layer(l, t(L["wg"]), t(L["wu"]), t(L["wd"]), t(L["sg"]), t(L["su"]), t(L["sd"]))
 
 
+@pytest.mark.parametrize("gather_kernel", [True, False])
 @pytest.mark.parametrize("hidden,inter,n_layers", [(256, 512, 3), (3072, 8192, 2)])
-def test_fused_world1_matches_plain(b2g, orc, syn, cuda, hidden, inter, n_layers):
+def test_fused_world1_matches_plain(b2g, orc, syn, cuda, hidden, inter, n_layers, gather_kernel):
+    """The fused exchange (rows summed by the separate gather kernel, or by the
+    gate||up launch in GATHER mode) gives bitwise the rows of the plain path."""
     tp = _tp(b2g)
     layers = _weights(orc, syn, hidden, inter, n_layers, 3000)
     plain = tp.TPStack(hidden, inter, n_layers, rank=0, world=1, max_m=8)
     fused = tp.TPStack(hidden, inter, n_layers, rank=0, world=1, max_m=8, fused=True)
+    fused.gather_kernel = gather_kernel
     _load_layers(plain, layers, cuda)
     _load_layers(fused, layers, cuda)
     fused.setup_comm(cuda)

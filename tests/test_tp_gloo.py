@@ -109,13 +109,15 @@ def test_tp_stack_gloo_ranks(b2g, orc, syn, tmp_path, world):
     assert r_full["rel_l2"] <= 5e-3, r_full
 
 
-def test_fused_exchange_schedule(b2g, monkeypatch):
+@pytest.mark.parametrize("gather_kernel", [True, False])
+def test_fused_exchange_schedule(b2g, monkeypatch, gather_kernel):
     """TPStack(fused=True)'s launch order on one rank, with recording stand-ins
-    for the ops: layer 0 stages h plainly; every later gate||up gathers the
-    previous push from its buffer (and writes h); push number r (counted over
-    all calls) goes to buffer r % 2, with the residual on rank 0 only; one
-    final gather reads the last push's buffer.  Each launch prefetches the next one's
-    weights."""
+    for the ops: layer 0 stages h plainly; before every later gate||up the
+    previous push is summed into h -- by the separate gather kernel followed
+    by a plain gate||up (default), or by the gate||up launch itself in GATHER
+    mode; push number r (counted over all calls) goes to buffer r % 2, with
+    the residual on rank 0 only; one final gather reads the last push's
+    buffer.  Each GEMV launch prefetches the next one's weights."""
     tp_mod = __import__("b2g.tp", fromlist=["TPStack"])
     calls = []
 
@@ -135,11 +137,20 @@ def test_fused_exchange_schedule(b2g, monkeypatch):
             pf = kw.get("prefetch")
             calls.append((self.name, mode, buf, packed, None if pf is None else pf[1]))
 
-    monkeypatch.setattr(tp_mod, "tp_gather", lambda comm, buf, op, hh: calls.append(("final", "gather", buf, None, None)))
+    def gather(comm, buf, op, hh):
+        assert comm is st.comm and op is st.down and hh is h
+        calls.append(("tp_gather", buf))
+    monkeypatch.setattr(tp_mod, "tp_gather", gather)
     G, Pu = tp_mod.TP_GATHER, tp_mod.TP_PUSH
+
+    def gu(layer, buf):  # the gate||up of a layer > 0 and the gather before it
+        if gather_kernel:
+            return [("tp_gather", buf), ("gu", "plain", None, f"pgu{layer}", f"pd{layer}")]
+        return [("gu", G, buf, f"pgu{layer}", f"pd{layer}")]
     for rank in (0, 1):
         calls.clear()
         st = tp_mod.TPStack(64, 128, 3, rank=rank, world=2, build_ops=False, fused=True)
+        st.gather_kernel = gather_kernel
         st.gate_up, st.down = Rec("gu"), Rec("dn")
         st.layers = [(f"pgu{l}", f"sgu{l}", f"pd{l}", f"sd{l}") for l in range(3)]
         h, act = torch.zeros(4, 64, dtype=torch.float16), torch.zeros(4, 64, dtype=torch.float16)
@@ -147,16 +158,14 @@ def test_fused_exchange_schedule(b2g, monkeypatch):
             st.enqueue(h, act, None)
         st.comm = object()
         st.enqueue(h, act, None)
-        assert calls == [("gu", "plain", None, "pgu0", "pd0"), ("dn", Pu, 0, "pd0", "pgu1"),
-                         ("gu", G, 0, "pgu1", "pd1"), ("dn", Pu, 1, "pd1", "pgu2"),
-                         ("gu", G, 1, "pgu2", "pd2"), ("dn", Pu, 0, "pd2", "pgu0"),
-                         ("final", "gather", 0, None, None)], rank
+        assert calls == ([("gu", "plain", None, "pgu0", "pd0"), ("dn", Pu, 0, "pd0", "pgu1")] + gu(1, 0) +
+                         [("dn", Pu, 1, "pd1", "pgu2")] + gu(2, 1) +
+                         [("dn", Pu, 0, "pd2", "pgu0"), ("tp_gather", 0)]), rank
         # A second call continues the alternation: with 3 layers the first
         # push of this call goes to buffer 1, not to buffer 0, which a peer's
         # final gather of the previous call may still be reading.
         calls.clear()
         st.enqueue(h, act, None)
-        assert calls == [("gu", "plain", None, "pgu0", "pd0"), ("dn", Pu, 1, "pd0", "pgu1"),
-                         ("gu", G, 1, "pgu1", "pd1"), ("dn", Pu, 0, "pd1", "pgu2"),
-                         ("gu", G, 0, "pgu2", "pd2"), ("dn", Pu, 1, "pd2", "pgu0"),
-                         ("final", "gather", 1, None, None)], rank
+        assert calls == ([("gu", "plain", None, "pgu0", "pd0"), ("dn", Pu, 1, "pd0", "pgu1")] + gu(1, 1) +
+                         [("dn", Pu, 0, "pd1", "pgu2")] + gu(2, 0) +
+                         [("dn", Pu, 1, "pd2", "pgu0"), ("tp_gather", 1)]), rank
