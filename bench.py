@@ -169,23 +169,15 @@ def adjacent_shapes(b2g, torch, device, M: int, reps: int = 5) -> dict:
         y = torch.empty(M, N, dtype=torch.float16, device=device)
         ws = op.workspace(device)
 
-        def sweep():
-            for i, p in enumerate(packs):
-                op.enqueue(x, p, s, y=y, workspace=ws, pdl=True, prefetch=(op, packs[(i + 1) % len(packs)]))
-        for _ in range(3):
-            sweep()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            sweep()
-        e1.record()
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / (reps * len(packs))
+        launches = [(lambda i=i, p=p: op.enqueue(x, p, s, y=y, workspace=ws, pdl=True,
+                                                 prefetch=(op, packs[(i + 1) % len(packs)])))
+                    for i, p in enumerate(packs)]
+        passes = max(2, -(-56 // len(packs)))
+        us = _chain_us(torch, launches, reps, passes)
         alg = op.packed_bytes() + 4 * N + 2 * M * K + 2 * M * N
         out[name] = {"K": K, "N": N, "m": M, "us_per_launch": round(us, 3), "alg_bytes": alg,
                      "achieved_gbs": round(alg / us / 1e3, 1), "grid": op.plan(M)["grid"],
-                     "launches_timed": reps * len(packs)}
+                     "launches_timed": reps * passes * len(packs), "timing": "CUDA graph replay"}
         del packs, base
     return out
 
@@ -196,21 +188,39 @@ def adjacent_shapes(b2g, torch, device, M: int, reps: int = 5) -> dict:
 # every launch streams from HBM), with programmatic dependent launch and the
 # L2 prefetch of the next launch's weights exactly as the stack chains them.
 # ---------------------------------------------------------------------------
-def _chain_us(torch, launches, reps: int) -> float:
-    """Device time per launch of a chain of launches (CUDA events on the
-    launching stream, after 3 warm-up passes)."""
+def _graph_of(torch, one_pass, passes: int = 1):
+    """A CUDA graph of `passes` calls of one_pass (after one eager call, so
+    plans and lazy state exist), replayed 3 times as warm-up.  Timing a graph
+    measures the device: eager launches through the Python binding take
+    longer to issue than a ~10 us GEMV takes to run."""
+    one_pass()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(passes):
+            one_pass()
     for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    return g
+
+
+def _chain_us(torch, launches, reps: int, passes: int = 2) -> float:
+    """Device time per launch of a chain of launches, replayed as a CUDA
+    graph of `passes` passes over the chain (CUDA events on the launching
+    stream, after 3 warm-up replays)."""
+    def one_pass():
         for f in launches:
             f()
-    torch.cuda.synchronize()
+    g = _graph_of(torch, one_pass, passes)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(reps):
-        for f in launches:
-            f()
+        g.replay()
     e1.record()
     torch.cuda.synchronize()
-    return e0.elapsed_time(e1) * 1e3 / (reps * len(launches))
+    g.reset()
+    return e0.elapsed_time(e1) * 1e3 / (reps * passes * len(launches))
 
 
 def gemv_bytes(K: int, N: int, M: int, wbytes: int, scale_bytes: int) -> int:
@@ -452,6 +462,7 @@ def run_ours(args):
         st = None
         tps = importlib.import_module("b2g.tp").TPStack(HIDDEN, INTER, LAYERS, rank=rank, world=world, max_m=M,
                                                         fused=args.tp_mode == "fused")
+        tps.exchange = args.tp_exchange
         gu_op, dn_op = tps.gate_up, tps.down
     pipe = {"auto": b2g.PIPE_AUTO, "registers": b2g.PIPE_REGISTERS, "tma": b2g.PIPE_TMA}[args.pipe]
     for op in (gu_op, dn_op):
@@ -588,18 +599,19 @@ def run_ours(args):
         for i, L in enumerate(layers):
             gu_op.enqueue(h, L["pgu"], L["sgu"], y=act, workspace=ws, pdl=True,
                           prefetch=(gu_op, layers[(i + 1) % LAYERS]["pgu"]))
-    for _ in range(3):
-        gu_sweep()
-    ms_gu = timed(gu_sweep, reps) / (reps * LAYERS)
+    g_gu = _graph_of(torch, gu_sweep)
+    ms_gu = timed(g_gu.replay, reps) / (reps * LAYERS)
+    g_gu.reset()
     achieved = gu_b / (ms_gu * 1e-3) / 1e9
     traffic = None
     tf = ROOT / "profiles" / "traffic.json"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(f"gate_up_m{M}_tp{tp}")
     gu_plan = gu_op.plan(M)
-    exch = 1 if tp > 1 and tps.fused else 0
+    # the gate||up launch carries the exchange only when it gathers the rows itself
+    exch = 1 if tp > 1 and tps.fused and tps.exchange == "gather_launch" else 0
     gu_kernel = (f"gemv_tma_kernel<2,1,{exch}>" if gu_plan["pipe"] == b2g.PIPE_TMA
-                 else f"gemv_streamk_kernel<2,1,0,{exch}>")
+                 else f"gemv_streamk_kernel<2,1,0,{3 if exch else 0}>")
     roofline = {"kernel": f"{gu_kernel} (RMSNorm + gate||up + SiLU*up)",
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "traffic": traffic,
@@ -610,9 +622,9 @@ def run_ours(args):
         for i, L in enumerate(layers):
             dn_op.enqueue(act, L["pd"], L["sd"], y=h, residual=h if rank == 0 else None,
                           workspace=ws, pdl=True, prefetch=(dn_op, layers[(i + 1) % LAYERS]["pd"]))
-    for _ in range(3):
-        dn_sweep()
-    ms_dn = timed(dn_sweep, reps) / (reps * LAYERS)
+    g_dn = _graph_of(torch, dn_sweep)
+    ms_dn = timed(g_dn.replay, reps) / (reps * LAYERS)
+    g_dn.reset()
 
     # ---- end to end through the C ABI with host buffers
     h_host = h0.cpu().pin_memory()
@@ -686,7 +698,9 @@ def run_ours(args):
                              f"fused gate||up 3072->2x8192 + SiLU*up -> down 8192->3072 + residual; "
                              f"E4M3 weights, per-channel FP32 scales, fp16 activations, fp32 accumulate"),
                 "hidden": HIDDEN, "intermediate": INTER, "layers": LAYERS, "m": M,
-                "parallelism": f"tp{tp}" + (f" ({args.tp_mode} all-reduce)" if tp > 1 else ""),
+                "parallelism": f"tp{tp}" + (f" ({args.tp_mode} all-reduce"
+                                            + (f", {args.tp_exchange} exchange" if args.tp_mode == "fused" else "")
+                                            + ")" if tp > 1 else ""),
                 "weights_per_step_bytes": bytes_rank * tp,
                 "l2": (f"inputs larger than L2: {bytes_rank * tp / 1e9:.2f} GB of weights streamed per step "
                        "(L2 126 MB), no flush"),
@@ -840,6 +854,8 @@ def main():
     ap.add_argument("--no-adjacent", action="store_true", help="skip timing qkv_proj / o_proj / lm_head")
     ap.add_argument("--tp-mode", choices=["fused", "nccl"], default="fused",
                     help="N > 1: all-reduce fused into the GEMVs over peer memory, or NCCL")
+    ap.add_argument("--tp-exchange", choices=["reduce", "gather_kernel", "gather_launch"], default="reduce",
+                    help="N > 1, fused: how the ranks' rows are summed (TPStack.exchange)")
     ap.add_argument("--pipe", choices=["auto", "registers", "tma"], default="auto",
                     help="how the GEMV launches feed their weights (B2G_OPT_PIPE)")
     ap.add_argument("--stack-mode", choices=["per_layer", "persistent", "persistent_tma"], default="per_layer",

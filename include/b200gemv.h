@@ -253,7 +253,19 @@ b2g_status b2g_enqueue_static(const b2g_op* op, const b2g_enqueue_args* args, b2
  * the reference runs on one GPU).  One process per GPU.  Each rank allocates
  * a zero-filled communication buffer of b2g_tp_comm_bytes(), shares it with
  * b2g_ipc_handle / b2g_ipc_open, and fills a b2g_tp_comm with every rank's
- * mapped addresses (b2g_tp_comm_layout).  Then, per layer:
+ * mapped addresses (b2g_tp_comm_layout).  Then, per layer, either
+ *   down op, mode REDUCE: the epilogue stores this rank's output rows into
+ *     its slot of every other rank's inbox as 8-byte words that carry the
+ *     launch's round number beside two fp16 values (so no fence and no
+ *     counter is needed); each CTA then polls (bounded) the words of its own
+ *     tiles from the other ranks -- the CTAs with the same index own the same
+ *     output tiles under the one plan -- and writes y = the sum in rank order
+ *     (fp32, one fp16 rounding; its own rows come from shared memory).  Every
+ *     rank ends the launch with the all-reduced rows; the next gate||up op is
+ *     a plain launch.  Needs whole tiles (K split 1, one CTA per tile),
+ *     16-byte-aligned x rows (ldx a multiple of 8, K a multiple of 32),
+ *     4-byte-aligned y rows, at most B2G_TP_MAX_CTAS CTAs and the register
+ *     pipeline.  Or
  *   down op, mode PUSH: instead of writing y, the epilogue stores this rank's
  *     output rows straight into its slot of every rank's inbox (NVLink peer
  *     stores); each CTA then fences at system scope once and adds one
@@ -262,11 +274,15 @@ b2g_status b2g_enqueue_static(const b2g_op* op, const b2g_enqueue_args* args, b2
  *     for all ranks' arrivals, sums the slots in rank order (fp32, one fp16
  *     rounding: every rank gets bitwise the same rows) and writes the sum to
  *     h_out (the residual input of the next down op).
- * After the last layer b2g_tp_gather writes the final rows.  Consecutive
- * layers alternate between the inbox's two buffers (`buf`).  A wait that
+ * and after the last layer b2g_tp_gather writes the final rows.  Consecutive
+ * layers alternate between the inbox's two buffers (`buf`): a rank writes a
+ * buffer again two exchanges later, after every rank has arrived in the
+ * exchange between, which each rank does only after its reads of the
+ * earlier one.  A wait that
  * expires sets the device error word (B2G_ERR_PEER_TIMEOUT class, code 4);
  * while the word is set, later waits give up at once (a lost peer costs one
- * 2 s wait, not one per layer).  b2g_tp_gather then leaves h as it was, and
+ * 2 s wait, not one per layer).  A REDUCE CTA then writes none of its
+ * rows of y, b2g_tp_gather leaves h as it was, and
  * a GATHER launch writes neither h_out nor its own output rows (its tiles'
  * split-K handshakes still complete, so the workspace stays consistent).
  * Every row produced since the error is invalid: read and clear the word
@@ -274,7 +290,8 @@ b2g_status b2g_enqueue_static(const b2g_op* op, const b2g_enqueue_args* args, b2
  * workspaces (b2g_workspace_init) before the next step.
  * ------------------------------------------------------------------------ */
 #define B2G_TP_MAX_RANKS 8
-enum { B2G_TP_NONE = 0, B2G_TP_PUSH = 1, B2G_TP_GATHER = 2 };
+#define B2G_TP_MAX_CTAS 256 /* REDUCE: CTAs per launch */
+enum { B2G_TP_NONE = 0, B2G_TP_PUSH = 1, B2G_TP_GATHER = 2, B2G_TP_REDUCE = 3 };
 typedef struct {
   int32_t world, rank;
   int32_t max_m;   /* rows per inbox slot */
@@ -283,9 +300,14 @@ typedef struct {
   void* counters[B2G_TP_MAX_RANKS]; /* every rank's arrival counters */
   void* epoch;                      /* this rank's launch counter */
 } b2g_tp_comm;
-/* Bytes of one rank's communication buffer (inbox [2][world][max_m][width]
- * fp16, counters [world] u32, epoch u32), and the addresses inside a buffer
- * at `base` (the same layout on every rank). */
+/* Bytes of one rank's communication buffer, and the addresses inside a
+ * buffer at `base` (the same layout on every rank): the inbox (PUSH and
+ * GATHER: [2][world][max_m][width] fp16; REDUCE: [2][world][max_m][width/2]
+ * 8-byte words); the counter region (PUSH counters [world] u32); the epoch
+ * region (epoch u32, then from byte 256 the REDUCE per-CTA launch counts
+ * [B2G_TP_MAX_CTAS] u32).  `counters` and `epoch` point at the starts of the
+ * two regions.  The buffer is zero-filled before first use and re-zeroed
+ * after an expired wait (every region, the counts included). */
 size_t b2g_tp_comm_bytes(int32_t world, int32_t max_m, int32_t width);
 b2g_status b2g_tp_comm_layout(void* base, int32_t world, int32_t max_m, int32_t width, void** inbox,
                               void** counters, void** epoch);
@@ -297,8 +319,9 @@ b2g_status b2g_tp_comm_layout(void* base, int32_t world, int32_t max_m, int32_t 
 b2g_status b2g_ipc_handle(const void* dev_ptr, void* record);
 b2g_status b2g_ipc_open(const void* record, void** dev_ptr);
 b2g_status b2g_ipc_close(void* dev_ptr);
-/* b2g_enqueue_ex with an exchange mode.  PUSH: the op must not fuse gate||up;
- * args->y is not written.  GATHER: the op's rows must be whole (K split 1),
+/* b2g_enqueue_ex with an exchange mode.  REDUCE: as PUSH, and args->y
+ * receives the all-reduced rows (requirements above; push_op is ignored).
+ * PUSH: the op must not fuse gate||up; args->y is not written.  GATHER: the op's rows must be whole (K split 1),
  * K == comm->width; args->x is not read; push_op is the op whose launches push
  * (its CTA count is the arrival count per round); h_out [m, ldh] receives the
  * summed rows. */

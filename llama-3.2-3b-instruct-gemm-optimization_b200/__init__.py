@@ -74,8 +74,9 @@ class StackFields(ctypes.Structure):
                 ("rms_eps", ctypes.c_float), ("tp_rank", ctypes.c_int32), ("tp_size", ctypes.c_int32)]
 
 
-TP_NONE, TP_PUSH, TP_GATHER = 0, 1, 2
+TP_NONE, TP_PUSH, TP_GATHER, TP_REDUCE = 0, 1, 2, 3
 TP_MAX_RANKS = 8
+TP_MAX_CTAS = 256
 
 
 class TpComm(ctypes.Structure):
@@ -255,8 +256,10 @@ class GemvOp:
     def enqueue_tp(self, comm, mode, buf, x, packed, scales=None, y=None, workspace=None, residual=None,
                    rms_eps: float = 1e-5, pdl: bool = False, stream=None, prefetch=None, push_op=None,
                    h_out=None):
-        """b2g_enqueue_tp: PUSH (this op's rows to every rank's inbox) or GATHER
-        (stage the all-reduced rows from the local inbox, writing them to h_out)."""
+        """b2g_enqueue_tp: REDUCE (this op's rows to every rank's inbox, then
+        y = the all-reduced rows on every rank), PUSH (the rows to every
+        rank's inbox only) or GATHER (stage the all-reduced rows from the
+        local inbox, writing them to h_out)."""
         m = x.shape[0]
         a = EnqueueArgs(m, x.data_ptr(), _rows_stride(x), packed.data_ptr(),
                         0 if scales is None else scales.data_ptr(),

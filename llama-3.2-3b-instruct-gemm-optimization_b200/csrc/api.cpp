@@ -559,6 +559,12 @@ static b2g_status enqueue_impl(const b2g_op* op, const b2g_enqueue_args* a, cons
   // One contributor per output tile (no K split, no tile shared between
   // CTAs) and aligned rows: the lean kernel flavor.
   p.lean = op->ksplit == 1 && op->max_contrib == 1 && aligned(a->x, 16) && a->ldx % 8 == 0 && op->K % 32 == 0;
+  if (tp && tp->mode == kTpReduce) {
+    // The REDUCE flavor is the lean one: whole tiles, aligned rows; y takes
+    // 4-byte pieces; one round count per CTA; register pipeline only.
+    if (!p.lean || p.grid > kTpMaxCtas || !aligned(a->y, 4) || a->ldy % 2 != 0) return B2G_ERR_INVALID;
+    if (use_tma(op, lp)) return B2G_ERR_UNSUPPORTED;
+  }
   if (use_tma(op, lp)) {
     p.off_ring = lp.off_ring;
     p.n_stages = lp.n_stages;
@@ -652,13 +658,22 @@ b2g_status b2g_enqueue_static(const b2g_op* op, const b2g_enqueue_args* args, b2
 // ---------------------------------------------------------------------------
 // Tensor-parallel exchange through peer memory
 // ---------------------------------------------------------------------------
+// The inbox holds either mode's buffers: PUSH / GATHER [2][world][max_m][width]
+// fp16, REDUCE [2][world][max_m][width / 2] u64 (twice the bytes).
 static size_t tp_inbox_bytes(int world, int max_m, int width) {
-  return ((size_t)2 * world * max_m * width * 2 + 255) / 256 * 256;
+  return ((size_t)2 * world * max_m * (width / 2) * 8 + 255) / 256 * 256;
 }
+
+// After the inbox: the counter region (PUSH counters [world]), then the
+// epoch region (epoch at word 0, REDUCE per-CTA rounds [kTpMaxCtas] at word
+// kTpRoundsOffset).
+static_assert(B2G_TP_MAX_CTAS == kTpMaxCtas, "REDUCE CTA limit");
+constexpr size_t kTpCounterRegion = 256;
+constexpr size_t kTpEpochRegion = ((size_t)(kTpRoundsOffset + kTpMaxCtas) * 4 + 255) / 256 * 256;
 
 size_t b2g_tp_comm_bytes(int32_t world, int32_t max_m, int32_t width) {
   if (world < 1 || world > B2G_TP_MAX_RANKS || max_m < 1 || width < 8) return 0;
-  return tp_inbox_bytes(world, max_m, width) + 256 + 256;
+  return tp_inbox_bytes(world, max_m, width) + kTpCounterRegion + kTpEpochRegion;
 }
 
 b2g_status b2g_tp_comm_layout(void* base, int32_t world, int32_t max_m, int32_t width, void** inbox,
@@ -668,7 +683,7 @@ b2g_status b2g_tp_comm_layout(void* base, int32_t world, int32_t max_m, int32_t 
   const size_t ib = tp_inbox_bytes(world, max_m, width);
   *inbox = b;
   *counters = b + ib;
-  *epoch = b + ib + 256;
+  *epoch = b + ib + kTpCounterRegion;
   return B2G_OK;
 }
 
@@ -763,13 +778,14 @@ static b2g_status fill_tp(const b2g_tp_comm* c, int mode, int buf, const b2g_op*
   tp->epoch = static_cast<unsigned*>(c->epoch);
   tp->h_out = static_cast<__half*>(h_out);
   tp->ldh = ldh;
+  tp->rounds = tp->epoch + kTpRoundsOffset;
   return B2G_OK;
 }
 
 b2g_status b2g_enqueue_tp(const b2g_op* op, const b2g_enqueue_args* a, const b2g_tp_comm* comm, int32_t mode,
                           int32_t buf, const b2g_op* push_op, void* h_out, int64_t ldh, b2g_stream_t stream) {
   if (!op || !a || !comm) return B2G_ERR_INVALID;
-  if (mode == B2G_TP_PUSH) {
+  if (mode == B2G_TP_PUSH || mode == B2G_TP_REDUCE) {
     if (op->planes != 1 || op->N != comm->width || op->N % kTileCh != 0) return B2G_ERR_INVALID;
     push_op = op;
   } else if (mode == B2G_TP_GATHER) {

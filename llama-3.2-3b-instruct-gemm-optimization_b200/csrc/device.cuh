@@ -192,6 +192,28 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
+// Single-copy-atomic 8-byte words at system scope: the flag-in-data exchange
+// (a 32-bit round number beside 32 bits of payload in one aligned word) needs
+// no fence, since a reader that sees the round sees the payload with it.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// 4 bytes global -> shared without holding a register (completes with
+// cp_async_wait_all in the issuing thread).
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\ncp.async.commit_group;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // float -> E4M3 code, round to nearest even, saturate to +-448.
 __device__ __forceinline__ uint8_t f32_to_e4m3(float f) {
   uint16_t r;

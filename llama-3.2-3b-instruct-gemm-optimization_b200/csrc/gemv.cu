@@ -198,6 +198,29 @@ __device__ __forceinline__ float rms_of(const GemvParams& p, const float* red, i
   return rsqrtf(s / (float)p.K + p.rms_eps);
 }
 
+// REDUCE: this launch's exchange round (this CTA's previous count, staged
+// in shared memory by thread 0, plus one).
+__device__ __forceinline__ unsigned tp_round() {
+  extern __shared__ __align__(1024) uint8_t dyn_smem[];
+  return *reinterpret_cast<volatile unsigned*>(dyn_smem + kOffRound) + 1u;
+}
+
+// REDUCE: a finished tile's rows (in the warp's stage) as flag-in-data
+// words (round << 32 | two channels) into this rank's slot of every other
+// rank's inbox (peer stores over NVLink); the rows stay in the stage for
+// this rank's own share of the sum.
+__device__ __noinline__ void tp_reduce_push(const GemvParams& p, const __half* stage, int tile, int lane) {
+  const unsigned long long flag = (unsigned long long)tp_round() << 32;
+  const int half_w = p.tp.width / 2;
+  for (int w = lane; w < p.M * 8; w += 32) {
+    const int m = w >> 3, i = w & 7;
+    const unsigned long long word = flag | *reinterpret_cast<const uint32_t*>(stage + m * 16 + 2 * i);
+    const size_t off = (((size_t)p.tp.buf * p.tp.world + p.tp.rank) * p.tp.inbox_m + m) * half_w + tile * 8 + i;
+    for (int r = 0; r < p.tp.world; ++r)
+      if (r != p.tp.rank) st_relaxed_sys_u64(reinterpret_cast<unsigned long long*>(p.tp.inbox[r]) + off, word);
+  }
+}
+
 // red: RMSNorm partial sums (nullptr when the op has no RMSNorm); the
 // normalisation is linear, so it scales the accumulator: y = fp16(acc * r_m * s_n).
 // stage: 256 B of this warp's own shared memory, for PUSH rows.  TPX: the
@@ -227,11 +250,15 @@ __device__ __forceinline__ void epilogue(const GemvParams& p, const Io& io, int 
         const float uf = __half2float(__float2half_rn(v[1][i] * r * e.scale[(j * 2 + 1) * 16 + c]));
         out = __float2half_rn(gf / (1.0f + __expf(-gf)) * uf);
       }
-      if (TPX && P == 1 && p.tp.mode == kTpPush)
+      if (TPX && P == 1 && tp_pushes(p.tp.mode))
         stage[m * 16 + c] = out;
       else
         io.y[(size_t)m * io.ldy + n] = out;
     }
+  }
+  if (TPX && P == 1 && p.tp.mode == kTpReduce) {
+    __syncwarp();
+    tp_reduce_push(p, stage, tile, lane);
   }
   if (TPX && P == 1 && p.tp.mode == kTpPush) {
     // The tile's rows are 32 B each: two lanes per row store 16 B into this
@@ -518,6 +545,78 @@ __device__ void gather_x(const GemvParams& p, __half* xs, int krange, int tid, f
   }
   if (red) reduce_rows(ss, tid, red);
 }
+
+// REDUCE tail (after every tile's epilogue; the CTA synchronised): the CTA
+// reads the words of its own tiles from the other ranks' slots of buffer
+// `buf` in its inbox, polling each (bounded) until it carries this launch's
+// round, and adds this rank's rows from the tiles' stages in rank order
+// (fp32 from 0, one fp16 rounding: the order tp_sum8 uses, so every rank
+// gets bitwise the same rows).  A CTA one of whose polls expires, or that
+// finds the error word set, writes none of its rows.  Tiles are whole (one
+// contributor each, K not split: host-checked), so tile j of the CTA's range
+// was finished by this CTA and its rows are in slot j's stage.
+__device__ __noinline__ void tp_reduce_tail(const GemvParams& p, uint8_t* smem, int tid) {
+  const unsigned v = tp_round();
+  const int u0 = range_start(p, blockIdx.x), u1 = range_start(p, blockIdx.x + 1);
+  const int t0 = fdiv(u0, p.div_kbpv);
+  const int nt = u1 > u0 ? fdiv(u1 - 1, p.div_kbpv) - t0 + 1 : 0;
+  const int per_tile = p.M * 8;  // 4-byte words (two channels) per tile
+  const int half_w = p.tp.width / 2;
+  bool expired = false;
+  float a0 = 0.f, a1 = 0.f;
+  int j = 0, m = 0, i = 0;
+  if (tid < nt * per_tile) {  // nt <= kMaxSlots, so at most kThreads words
+    j = tid / per_tile;
+    const int rem = tid - j * per_tile;
+    m = rem >> 3;
+    i = rem & 7;
+    const uint32_t own = *reinterpret_cast<const uint32_t*>(
+        reinterpret_cast<const __half*>(smem + kOffSlots + (size_t)j * kWarps * kUnitPlaneBytes) + m * 16 + 2 * i);
+    const unsigned long long* box = reinterpret_cast<const unsigned long long*>(p.tp.inbox[p.tp.rank]) +
+                                    (size_t)m * half_w + (t0 + j) * 8 + i;
+    unsigned long long t_start = 0;
+    for (int r = 0; r < p.tp.world && !expired; ++r) {
+      uint32_t d = own;
+      if (r != p.tp.rank) {
+        const unsigned long long* src = box + ((size_t)p.tp.buf * p.tp.world + r) * p.tp.inbox_m * half_w;
+        unsigned long long w = ld_relaxed_sys_u64(src);
+        while ((unsigned)(w >> 32) != v) {
+          if (t_start == 0) t_start = globaltimer_ns();
+          if (*reinterpret_cast<volatile int*>(p.error) != 0 || globaltimer_ns() - t_start > kWaitBudgetNs) {
+            expired = true;
+            break;
+          }
+          __nanosleep(32);
+          w = ld_relaxed_sys_u64(src);
+        }
+        d = (uint32_t)w;
+      }
+      const float2 f = h2_to_f2(d);
+      a0 += f.x;
+      a1 += f.y;
+    }
+  }
+  if (__syncthreads_or(expired)) {
+    if (tid == 0) atomicCAS(p.error, 0, kErrPeerWait);
+  } else if (tid < nt * per_tile) {
+    *reinterpret_cast<__half2*>(p.y + (size_t)m * p.ldy + (t0 + j) * kTileCh + 2 * i) = __floats2half2_rn(a0, a1);
+  }
+  if (tid == 0) {
+    volatile unsigned* rc = p.tp.rounds;
+    rc[blockIdx.x] = v;
+    if (blockIdx.x == 0)
+      for (int c = p.grid; c < kTpMaxCtas; ++c) rc[c] = v;  // every entry advances, whatever the grid
+  }
+}
+
+// REDUCE: thread 0 completes the copy of the CTA's round count into shared
+// memory (issued after the dependency wait) before the combine phase.
+struct RoundHook {
+  template <class T>
+  __device__ __forceinline__ void operator()(T&) const {
+    if (threadIdx.x == 0) cp_async_wait_all();
+  }
+};
 
 // ---------------------------------------------------------------------------
 // Per-unit math
@@ -886,13 +985,16 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
 // tensor-parallel PUSH epilogue compiled in) or kFlavorGather (the GATHER
 // staging compiled in).  Code size shows up as instruction-fetch stalls in
 // every launch, so each launch takes the smallest flavor that covers it.
-enum : int { kFlavorLean = 0, kFlavorGeneral = 1, kFlavorPush = 2, kFlavorGather = 3 };
+// kFlavorReduce: the lean flavor with the REDUCE epilogue and tail (one
+// plane only).
+enum : int { kFlavorLean = 0, kFlavorGeneral = 1, kFlavorPush = 2, kFlavorGather = 3, kFlavorReduce = 4 };
 
 template <int P, int WB, int MATH, int FLAVOR>
 __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_constant__ GemvParams p) {
-  constexpr bool TPX = FLAVOR == kFlavorPush;  // the PUSH epilogue and arrivals
+  constexpr bool REDUCEX = FLAVOR == kFlavorReduce;
+  constexpr bool TPX = FLAVOR == kFlavorPush || REDUCEX;  // the pushing epilogue and arrivals
   constexpr bool GATHERX = FLAVOR == kFlavorGather;
-  constexpr bool LEAN = FLAVOR == kFlavorLean;
+  constexpr bool LEAN = FLAVOR == kFlavorLean || REDUCEX;
   extern __shared__ __align__(1024) uint8_t smem[];
   // 128 KB of weights in flight per SM (16 B x 512 threads x 16); the FFMA
   // variant needs the registers for its accumulators and keeps half.
@@ -931,14 +1033,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_
   }
   pdl_wait();
   if (tid == 0) TRACE(1);
-  if (TPX && p.tp.mode == kTpPush && blockIdx.x == 0 && tid == 0) atomicAdd(p.tp.epoch, 1u);
-  run_phase<P, WB, MATH, R, NoHook, TPX, true, LEAN, GATHERX>(p, io_of_params(p), smem, ring, pol, NoHook{});
-  if (TPX && p.tp.mode == kTpPush) {
-    // This CTA's peer stores are done: one arrival on every rank.
-    __syncthreads();
-    if (tid == 0) {
-      fence_acq_rel_sys();  // the CTA's peer stores (ordered by the barrier) before the arrivals
-      for (int r = 0; r < p.tp.world; ++r) red_relaxed_sys_add(p.tp.counters[r] + p.tp.rank, 1u);
+  if constexpr (REDUCEX) {
+    // the previous launch's round count (that launch is complete now)
+    if (tid == 0) cp_async4(smem + kOffRound, p.tp.rounds + blockIdx.x);
+    run_phase<P, WB, MATH, R, RoundHook, TPX, true, LEAN, GATHERX>(p, io_of_params(p), smem, ring, pol, RoundHook{});
+    __syncthreads();  // every tile's rows staged and pushed
+    tp_reduce_tail(p, smem, tid);
+  } else {
+    if (TPX && p.tp.mode == kTpPush && blockIdx.x == 0 && tid == 0) atomicAdd(p.tp.epoch, 1u);
+    run_phase<P, WB, MATH, R, NoHook, TPX, true, LEAN, GATHERX>(p, io_of_params(p), smem, ring, pol, NoHook{});
+    if (TPX && p.tp.mode == kTpPush) {
+      // This CTA's peer stores are done: one arrival on every rank.
+      __syncthreads();
+      if (tid == 0) {
+        fence_acq_rel_sys();  // the CTA's peer stores (ordered by the barrier) before the arrivals
+        for (int r = 0; r < p.tp.world; ++r) red_relaxed_sys_add(p.tp.counters[r] + p.tp.rank, 1u);
+      }
     }
   }
   if (tid == 0) TRACE(4);
@@ -1458,6 +1568,8 @@ cudaError_t launch_variant(const GemvParams& p, size_t smem, bool pdl, cudaStrea
   // layer (28 layers, M = 8 / 1): gate||up on the exchange flavor 22.9 /
   // 22.1 us, on the general one 21.2 / 20.5, both ops on the lean one
   // 20.6 / 19.6.
+  if constexpr (P == 1)
+    if (p.tp.mode == kTpReduce) return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, kFlavorReduce>, p);
   if (p.tp.mode == kTpPush) return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, kFlavorPush>, p);
   if (p.tp.mode == kTpGather) return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, kFlavorGather>, p);
   if (p.lean) return cudaLaunchKernelEx(&cfg, gemv_streamk_kernel<P, WB, MATH, kFlavorLean>, p);
@@ -1598,6 +1710,10 @@ cudaError_t gemv_set_smem_limit(int bytes) {
   B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, kFlavorGeneral>))
   B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, kFlavorPush>))
   B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, kFlavorGather>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathMma, kFlavorReduce>))
+  B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, kFlavorReduce>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathMma, kFlavorReduce>))
+  B2G_LIM((gemv_streamk_kernel<1, 2, kMathFfma, kFlavorReduce>))
   B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, kFlavorLean>))
   B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, kFlavorGeneral>))
   B2G_LIM((gemv_streamk_kernel<1, 1, kMathFfma, kFlavorPush>))

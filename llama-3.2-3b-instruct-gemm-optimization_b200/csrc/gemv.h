@@ -23,12 +23,13 @@ constexpr int kWarps = 16;  // one CTA of 16 warps per SM
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxSlots = 8;  // virtual tiles one CTA may touch
 constexpr int kRing = 16;     // uint4 registers per lane for in-flight weight units
-// Shared memory: [64,68) barrier verdict, [128,640) RMSNorm sums of squares
+// Shared memory: [64,68) barrier verdict, [68,72) REDUCE round, [128,640) RMSNorm sums of squares
 // [16 warps][8 rows], then the per-warp partial slots
 // [n_slots][warps][planes][32 lanes][16 B], then the per-slot epilogue inputs
 // (scales [n_slots][planes][16], residual rows [n_slots][8][16], fp32), then
 // the x rows.
 constexpr int kOffMisc = 64;
+constexpr int kOffRound = 68;  // REDUCE: this CTA's previous round (u32)
 constexpr int kOffRed = 128;
 constexpr int kOffBars = 640;  // TMA pipeline: full[kMaxStages] then empty[kMaxStages] mbarriers
 constexpr int kMaxStages = 24;
@@ -55,8 +56,20 @@ enum MathKind : int { kMathMma = 0, kMathFfma = 1 };
 // activation staging waits (bounded) until every counter reaches
 // epoch * push_grid, then sums slots 0..world-1 of buffer `buf` in rank order
 // (fp32, one fp16 rounding) and writes the sum to h_out as it stages it.
+// REDUCE: flag-in-data words.  The epilogue stores each finished tile's rows
+// into slot `rank` of buffer `buf` of every other rank's REDUCE inbox
+// [2][world][max_m][width / 2] u64, each 8-byte word = (round << 32) | two
+// fp16; then every CTA reads the words of its own tiles from the other
+// ranks' slots (bounded polls until the round matches: the CTAs with the
+// same index own the same tiles under the one plan), adds its own rows from
+// shared memory in rank order and writes the sums to y.  Every rank ends the
+// launch with the all-reduced rows, with no fence and no counters.  The round
+// is the launch count kept per CTA index in this rank's memory (all
+// kTpMaxCtas entries advance together, whatever the grid).
 constexpr int kMaxTp = 8;
-enum TpMode : int { kTpNone = 0, kTpPush = 1, kTpGather = 2 };
+constexpr int kTpMaxCtas = 256;       // REDUCE: CTAs per launch
+constexpr int kTpRoundsOffset = 64;   // u32 words from this rank's epoch to its per-CTA rounds
+enum TpMode : int { kTpNone = 0, kTpPush = 1, kTpGather = 2, kTpReduce = 3 };
 struct TpParams {
   int mode;
   int world, rank;
@@ -69,7 +82,10 @@ struct TpParams {
   unsigned* epoch;           // this rank's count of pushing launches
   __half* h_out;             // GATHER: the reduced rows [m, ldh] (this rank's memory)
   long long ldh;
+  unsigned* rounds;          // REDUCE: this rank's per-CTA launch counts [kTpMaxCtas]
 };
+
+__host__ __device__ inline bool tp_pushes(int mode) { return mode == kTpPush || mode == kTpReduce; }
 
 // Division of x < 2^31 by a divisor fixed per launch, as a multiply-high and
 // a shift (Granlund & Montgomery, "Division by invariant integers using

@@ -15,17 +15,25 @@ the reference runs on one GPU):
 RMSNorm runs replicated (each rank normalises the same h).  The GEMVs run in
 the C-ABI library (``GemvOp``).  The all-reduce is either
 torch.distributed's (NCCL on GPUs), or -- ``fused=True`` -- fused into the
-launches through peer memory: the down GEMV's epilogue stores its rows into
-every rank's inbox over NVLink (b2g_enqueue_tp, PUSH), and before the next
-layer's gate||up GEMV a small kernel (b2g_tp_gather) waits for every rank's
-arrivals and sums the inbox slots in rank order into h (or, with
-``gather_kernel = False``, the gate||up GEMV sums them itself while it stages
-its activations: b2g_enqueue_tp, GATHER).
+down launch through peer memory (``exchange``):
+
+* "reduce" (default, b2g_enqueue_tp REDUCE): the down GEMV's epilogue stores
+  its rows into every rank's inbox over NVLink, each CTA waits for the CTAs
+  with its index on the other ranks (they own the same output tiles) and sums
+  its tiles' slots in rank order into h; the next gate||up is a plain launch;
+* "gather_kernel" (PUSH, then b2g_tp_gather): the down launch only pushes;
+  before the next gate||up a small kernel waits for every rank's arrivals
+  and sums the slots into h;
+* "gather_launch" (PUSH, then GATHER): the gate||up launch sums the slots
+  itself while it stages its activations.
 """
 from __future__ import annotations
 
 from . import (FUSE_GATE_UP_SILU, FUSE_NONE, FUSE_RESIDUAL_ADD, FUSE_RMSNORM_INPUT, TP_GATHER, TP_PUSH,
-               GemvOp, TpComm, ipc_close, ipc_handle, ipc_open, tp_comm_bytes, tp_comm_layout, tp_gather)
+               TP_REDUCE, GemvOp, TpComm, ipc_close, ipc_handle, ipc_open, tp_comm_bytes, tp_comm_layout,
+               tp_gather)
+
+EXCHANGES = ("reduce", "gather_kernel", "gather_launch")
 
 
 def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
@@ -54,13 +62,11 @@ class TPStack:
         self.layers = [None] * n_layers
         self.gate_up = self.down = None
         self.fused = fused
-        # Fused exchange: sum the ranks' rows in a separate small kernel
-        # (b2g_tp_gather) before each plain gate||up launch (default), or
-        # inside every gate||up CTA (False: the GATHER launch mode).  Measured
-        # on one B200 with world = 1 (28 layers, M = 8): 27.8 against 30.5 us
-        # per layer -- the gate||up launch keeps its lean code, and the rows
-        # are summed once per rank instead of once per CTA.
-        self.gather_kernel = True
+        # Fused exchange (one of EXCHANGES).  Measured on one B200 with
+        # world = 1 (28 layers, M = 8): gather_kernel 27.8 us per layer,
+        # gather_launch 30.5 (the gate||up launch loses its lean code and
+        # every CTA sums the rows).
+        self.exchange = "reduce"
         # Exchange rounds pushed so far (one per layer, carried across calls):
         # round r uses inbox buffer r % 2, so consecutive pushes always
         # alternate, also from the last layer of one call to the first of the next.
@@ -188,12 +194,25 @@ class TPStack:
             # replays would not alternate (the last push of one replay and the
             # first of the next would share a buffer a peer may still read).
             raise ValueError(f"a CUDA graph of the fused exchange needs an even layer count, not {n}")
+        if self.exchange not in EXCHANGES:
+            raise ValueError(f"exchange {self.exchange!r} is not one of {EXCHANGES}")
+        if self.exchange == "reduce":
+            for layer in range(n):
+                pgu, sgu, pd, sd = self.layers[layer]
+                nxt = self.layers[(layer + 1) % n]
+                self.gate_up.enqueue(h, pgu, sgu, y=act, workspace=workspace, rms_eps=self.rms_eps, pdl=True,
+                                     prefetch=(self.down, pd))
+                self.down.enqueue_tp(self.comm, TP_REDUCE, self._round % 2, act, pd, sd, y=h, workspace=workspace,
+                                     residual=h if self.rank == 0 else None, pdl=True,
+                                     prefetch=None if nxt is None else (self.gate_up, nxt[0]))
+                self._round += 1
+            return h
         for layer in range(n):
             pgu, sgu, pd, sd = self.layers[layer]
             if layer == 0:
                 self.gate_up.enqueue(h, pgu, sgu, y=act, workspace=workspace, rms_eps=self.rms_eps, pdl=True,
                                      prefetch=(self.down, pd))
-            elif self.gather_kernel:
+            elif self.exchange == "gather_kernel":
                 # h = sum of the ranks' previous down outputs, then a plain gate||up
                 tp_gather(self.comm, (self._round - 1) % 2, self.down, h)
                 self.gate_up.enqueue(h, pgu, sgu, y=act, workspace=workspace, rms_eps=self.rms_eps, pdl=True,

@@ -1,7 +1,8 @@
 """The all-reduce fused into the GEMVs through peer memory (b2g_enqueue_tp).
 
-* world = 1 on one GPU: the push/gather path (inbox slot, arrival counters,
-  epoch, final gather) must give bitwise the rows of the plain path;
+* world = 1 on one GPU: every fused exchange (REDUCE; PUSH with the gather
+  kernel; PUSH with GATHER launches) must give bitwise the rows of the plain
+  path;
 * a wait that nothing satisfies expires (bounded) and reports through the
   device error word, leaving the rows untouched;
 * two ranks on two GPUs, and every GPU of the machine (up to 8) when it
@@ -43,16 +44,17 @@ def _load_layers(st, layers, dev):
         st.prepack_layer(l, t(L["wg"]), t(L["wu"]), t(L["wd"]), t(L["sg"]), t(L["su"]), t(L["sd"]))
 
 
-@pytest.mark.parametrize("gather_kernel", [True, False])
+@pytest.mark.parametrize("exchange", ["reduce", "gather_kernel", "gather_launch"])
 @pytest.mark.parametrize("hidden,inter,n_layers", [(256, 512, 3), (3072, 8192, 2)])
-def test_fused_world1_matches_plain(b2g, orc, syn, cuda, hidden, inter, n_layers, gather_kernel):
-    """The fused exchange (rows summed by the separate gather kernel, or by the
-    gate||up launch in GATHER mode) gives bitwise the rows of the plain path."""
+def test_fused_world1_matches_plain(b2g, orc, syn, cuda, hidden, inter, n_layers, exchange):
+    """The fused exchange (rows summed by each down CTA after its counterparts
+    arrive, by the separate gather kernel, or by the gate||up launch in GATHER
+    mode) gives bitwise the rows of the plain path."""
     tp = _tp(b2g)
     layers = _weights(orc, syn, hidden, inter, n_layers, 3000)
     plain = tp.TPStack(hidden, inter, n_layers, rank=0, world=1, max_m=8)
     fused = tp.TPStack(hidden, inter, n_layers, rank=0, world=1, max_m=8, fused=True)
-    fused.gather_kernel = gather_kernel
+    fused.exchange = exchange
     _load_layers(plain, layers, cuda)
     _load_layers(fused, layers, cuda)
     fused.setup_comm(cuda)
@@ -99,6 +101,79 @@ def test_gather_wait_expires(b2g, orc, syn, cuda):
     st.close_comm()
 
 
+def test_reduce_wait_expires_writes_nothing(b2g, orc, syn, cuda):
+    """A down launch in REDUCE mode whose peer never writes: rank 0 of a
+    two-rank exchange whose rank 1 is a second buffer on this GPU that no
+    launch fills.  Every poll gives up after the bounded wait, records the
+    peer-wait code, and y is left as it was; while the error word is set, a
+    later launch gives up at once.  After the word is cleared and the buffers
+    re-zeroed, the same op gives the plain result at world 1."""
+    tp = _tp(b2g)
+    H, I = 256, 512
+    nbytes = b2g.tp_comm_bytes(2, 8, H)
+    bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=cuda) for _ in range(2)]
+    comm = b2g.TpComm()
+    comm.world, comm.rank, comm.max_m, comm.width = 2, 0, 8, H
+    for r, b in enumerate(bufs):
+        inbox, counters, epoch = b2g.tp_comm_layout(b.data_ptr(), 2, 8, H)
+        comm.inbox[r], comm.counters[r] = inbox, counters
+        if r == 0:
+            comm.epoch = epoch
+    st = tp.TPStack(H, I, 1, rank=0, world=1, max_m=8, fused=True)
+    wd, sd = b2g.quantize_e4m3(torch.from_numpy(syn.weights(83, I, H)).to(cuda), "channel_fp32")
+    pd = st.down.prepack(wd)
+    act = torch.from_numpy(syn.activations(84, 2, I)).to(cuda)
+    h = torch.full((2, H), 3.0, dtype=torch.float16, device=cuda)
+    ws = st.workspace(cuda)
+    st.down.enqueue_tp(comm, b2g.TP_REDUCE, 0, act, pd, sd, y=h, residual=h, workspace=ws)
+    torch.cuda.synchronize()
+    assert b2g.device_error(clear=False) == 4  # peer wait expired
+    assert bool((h == 3.0).all())
+    t0 = time.perf_counter()
+    st.down.enqueue_tp(comm, b2g.TP_REDUCE, 1, act, pd, sd, y=h, residual=h, workspace=ws)
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 0.5
+    assert b2g.device_error(clear=True) == 4
+    assert bool((h == 3.0).all())
+    # recovery: the word cleared, the exchange buffer re-zeroed
+    one = st.setup_comm(cuda)
+    st.down.enqueue_tp(one, b2g.TP_REDUCE, 0, act, pd, sd, y=h, residual=h, workspace=ws)
+    torch.cuda.synchronize()
+    want = 3.0 + orc.gemv(wd.cpu().numpy(), orc.WTYPE_FP8, act.cpu().numpy(), orc.SCALE_CHANNEL_FP32,
+                          sd.cpu().numpy())
+    assert orc.compare(h.cpu().numpy(), want)["rel_l2"] <= 5e-3
+    assert b2g.device_error() == 0
+    st.close_comm()
+
+
+def test_reduce_refuses_unfit_plans(b2g, cuda):
+    """REDUCE needs whole tiles and the register pipeline: a K-split down op
+    and the TMA pipeline are refused before anything is launched."""
+    tp = _tp(b2g)
+    H, I = 256, 512
+    st = tp.TPStack(H, I, 1, rank=0, world=1, max_m=8, fused=True)
+    comm = st.setup_comm(cuda)
+    act = torch.zeros(2, I, dtype=torch.float16, device=cuda)
+    h = torch.zeros(2, H, dtype=torch.float16, device=cuda)
+    ws = st.workspace(cuda)
+    st.down.set_option(b2g.OPT_PIPE, b2g.PIPE_TMA)
+    pd = st.down.prepack(torch.zeros(I, H, dtype=torch.uint8, device=cuda))
+    sd = torch.ones(H, dtype=torch.float32, device=cuda)
+    with pytest.raises(b2g.B2GError) as e:
+        st.down.enqueue_tp(comm, b2g.TP_REDUCE, 0, act, pd, sd, y=h, residual=h, workspace=ws)
+    assert e.value.status == b2g.ERR_UNSUPPORTED
+    split = b2g.GemvOp(I, H, max_m=8, fuse=b2g.FUSE_RESIDUAL_ADD)
+    split.set_option(b2g.OPT_KSPLIT, 2)
+    assert split.plan(2)["ksplit"] == 2
+    ps = split.prepack(torch.zeros(I, H, dtype=torch.uint8, device=cuda))
+    with pytest.raises(b2g.B2GError) as e:
+        split.enqueue_tp(comm, b2g.TP_REDUCE, 0, act, ps, sd, y=h, residual=h, workspace=split.workspace(cuda))
+    assert e.value.status == b2g.ERR_INVALID
+    torch.cuda.synchronize()
+    assert bool((h == 0).all()) and b2g.device_error() == 0
+    st.close_comm()
+
+
 @pytest.mark.parametrize("pipe", ["registers", "tma"])
 def test_gather_gemv_wait_expires_writes_nothing(b2g, orc, syn, cuda, pipe):
     """A gate||up launch in GATHER mode whose wait for the peers' arrivals
@@ -141,7 +216,7 @@ def test_gather_gemv_wait_expires_writes_nothing(b2g, orc, syn, cuda, pipe):
 HID, INT, NL, MM = 3072, 8192, 2, 8
 
 
-def _rank(rank, world, port, out, nl=NL, steps=1):
+def _rank(rank, world, port, out, nl=NL, steps=1, exchange="reduce"):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
@@ -151,6 +226,7 @@ def _rank(rank, world, port, out, nl=NL, steps=1):
     tp = __import__("b2g.tp", fromlist=["TPStack"])
     layers = _weights(orc, syn, HID, INT, nl, 4000)
     st = tp.TPStack(HID, INT, nl, rank=rank, world=world, max_m=8, fused=True)
+    st.exchange = exchange
     _load_layers(st, layers, dev)
     st.setup_comm(dev)
     h = torch.from_numpy(syn.hidden_state(MM, HID)).to(dev)
@@ -177,8 +253,10 @@ def _port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("which,nl,steps", [("two", NL, 1), ("two", 2, 2), ("two", 3, 2), ("all", NL, 1)])
-def test_fused_ranks(b2g, orc, syn, cuda, tmp_path, which, nl, steps):
+@pytest.mark.parametrize("which,nl,steps,exchange", [("two", NL, 1, "reduce"), ("two", 2, 2, "reduce"),
+                                                     ("two", 3, 2, "reduce"), ("two", 3, 2, "gather_kernel"),
+                                                     ("all", NL, 1, "reduce"), ("all", 2, 2, "gather_kernel")])
+def test_fused_ranks(b2g, orc, syn, cuda, tmp_path, which, nl, steps, exchange):
     """Every rank's rows bitwise equal and, on rank 0, the oracle's sharded
     stack, after each of `steps` consecutive steps (an odd layer count makes
     the second step start on the other inbox buffer)."""
@@ -188,7 +266,7 @@ def test_fused_ranks(b2g, orc, syn, cuda, tmp_path, which, nl, steps):
     world = 2 if which == "two" else n
     import torch.multiprocessing as mp
     out = str(tmp_path / "h")
-    mp.spawn(_rank, args=(world, _port(), out, nl, steps), nprocs=world, join=True)
+    mp.spawn(_rank, args=(world, _port(), out, nl, steps, exchange), nprocs=world, join=True)
     got = [np.load(out + f".{r}.npy") for r in range(world)]
     assert [open(out + f".{r}.err").read() for r in range(world)] == ["0"] * world
     for r in range(1, world):

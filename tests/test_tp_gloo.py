@@ -109,15 +109,17 @@ def test_tp_stack_gloo_ranks(b2g, orc, syn, tmp_path, world):
     assert r_full["rel_l2"] <= 5e-3, r_full
 
 
-@pytest.mark.parametrize("gather_kernel", [True, False])
-def test_fused_exchange_schedule(b2g, monkeypatch, gather_kernel):
+@pytest.mark.parametrize("exchange", ["reduce", "gather_kernel", "gather_launch"])
+def test_fused_exchange_schedule(b2g, monkeypatch, exchange):
     """TPStack(fused=True)'s launch order on one rank, with recording stand-ins
-    for the ops: layer 0 stages h plainly; before every later gate||up the
+    for the ops.  REDUCE (default): every layer is a plain gate||up and a down
+    launch in REDUCE mode writing h, nothing after the last layer.  The PUSH
+    exchanges: layer 0 stages h plainly; before every later gate||up the
     previous push is summed into h -- by the separate gather kernel followed
-    by a plain gate||up (default), or by the gate||up launch itself in GATHER
-    mode; push number r (counted over all calls) goes to buffer r % 2, with
-    the residual on rank 0 only; one final gather reads the last push's
-    buffer.  Each GEMV launch prefetches the next one's weights."""
+    by a plain gate||up, or by the gate||up launch itself in GATHER mode --
+    and one final gather reads the last push's buffer.  Exchange number r
+    (counted over all calls) goes to buffer r % 2, with the residual on rank 0
+    only.  Each GEMV launch prefetches the next one's weights."""
     tp_mod = __import__("b2g.tp", fromlist=["TPStack"])
     calls = []
 
@@ -141,16 +143,27 @@ def test_fused_exchange_schedule(b2g, monkeypatch, gather_kernel):
         assert comm is st.comm and op is st.down and hh is h
         calls.append(("tp_gather", buf))
     monkeypatch.setattr(tp_mod, "tp_gather", gather)
-    G, Pu = tp_mod.TP_GATHER, tp_mod.TP_PUSH
+    G, Pu, R = tp_mod.TP_GATHER, tp_mod.TP_PUSH, tp_mod.TP_REDUCE
 
     def gu(layer, buf):  # the gate||up of a layer > 0 and the gather before it
-        if gather_kernel:
+        if exchange == "gather_kernel":
             return [("tp_gather", buf), ("gu", "plain", None, f"pgu{layer}", f"pd{layer}")]
         return [("gu", G, buf, f"pgu{layer}", f"pd{layer}")]
+
+    def want(first_buf):
+        b = [first_buf, 1 - first_buf, first_buf]
+        if exchange == "reduce":
+            return [c for l in range(3) for c in (("gu", "plain", None, f"pgu{l}", f"pd{l}"),
+                                                   ("dn", R, b[l], f"pd{l}", f"pgu{(l + 1) % 3}"))]
+        return ([("gu", "plain", None, "pgu0", "pd0"), ("dn", Pu, b[0], "pd0", "pgu1")] + gu(1, b[0]) +
+                [("dn", Pu, b[1], "pd1", "pgu2")] + gu(2, b[1]) +
+                [("dn", Pu, b[2], "pd2", "pgu0"), ("tp_gather", b[2])])
     for rank in (0, 1):
         calls.clear()
         st = tp_mod.TPStack(64, 128, 3, rank=rank, world=2, build_ops=False, fused=True)
-        st.gather_kernel = gather_kernel
+        if exchange != "reduce":
+            st.exchange = exchange
+        assert st.exchange == exchange
         st.gate_up, st.down = Rec("gu"), Rec("dn")
         st.layers = [(f"pgu{l}", f"sgu{l}", f"pd{l}", f"sd{l}") for l in range(3)]
         h, act = torch.zeros(4, 64, dtype=torch.float16), torch.zeros(4, 64, dtype=torch.float16)
@@ -158,14 +171,13 @@ def test_fused_exchange_schedule(b2g, monkeypatch, gather_kernel):
             st.enqueue(h, act, None)
         st.comm = object()
         st.enqueue(h, act, None)
-        assert calls == ([("gu", "plain", None, "pgu0", "pd0"), ("dn", Pu, 0, "pd0", "pgu1")] + gu(1, 0) +
-                         [("dn", Pu, 1, "pd1", "pgu2")] + gu(2, 1) +
-                         [("dn", Pu, 0, "pd2", "pgu0"), ("tp_gather", 0)]), rank
+        assert calls == want(0), rank
         # A second call continues the alternation: with 3 layers the first
-        # push of this call goes to buffer 1, not to buffer 0, which a peer's
-        # final gather of the previous call may still be reading.
+        # exchange of this call goes to buffer 1, not to buffer 0, which a
+        # peer may still be reading from the previous call's last exchange.
         calls.clear()
         st.enqueue(h, act, None)
-        assert calls == ([("gu", "plain", None, "pgu0", "pd0"), ("dn", Pu, 1, "pd0", "pgu1")] + gu(1, 1) +
-                         [("dn", Pu, 0, "pd1", "pgu2")] + gu(2, 0) +
-                         [("dn", Pu, 1, "pd2", "pgu0"), ("tp_gather", 1)]), rank
+        assert calls == want(1), rank
+    st.exchange = "bogus"
+    with pytest.raises(ValueError, match="exchange"):
+        st.enqueue(h, act, None)
