@@ -141,8 +141,11 @@ __device__ __forceinline__ Epi epi_of(const GemvParams& p, uint8_t* smem, int P)
 }
 
 // The scales of the CTA's tiles (constants: may load before the previous
-// kernel is waited on).
-template <int P>
+// kernel is waited on).  ASYNC: FP32 per-channel scales go global -> shared
+// with cp.async, so no thread stalls on them before the dependency wait (a
+// load issued behind the start of the L2 prefetch waits microseconds); the
+// caller completes them (cp_async_wait_all) before the epilogue reads them.
+template <int P, bool ASYNC = false>
 __device__ __forceinline__ void load_scales(const GemvParams& p, const Io& io, const Epi& e, int vt_first, int nvt,
                                             int tid) {
   const int ns = nvt * P * 16;
@@ -150,7 +153,10 @@ __device__ __forceinline__ void load_scales(const GemvParams& p, const Io& io, c
     const int j = i / (P * 16), pl = (i / 16) % P, c = i % 16;
     const int tile = fdiv(vt_first + j, p.div_tiles);
     const int n = (vt_first + j - tile * p.n_tiles) * kTileCh + c;
-    e.scale[i] = n < p.N ? channel_scale(p, io, pl, n) : 0.f;
+    if (ASYNC && p.scale_mode == 3 && n < p.N)
+      cp_async4(e.scale + i, reinterpret_cast<const float*>(io.scales) + (size_t)pl * p.N + n);
+    else
+      e.scale[i] = n < p.N ? channel_scale(p, io, pl, n) : 0.f;
   }
 }
 
@@ -944,6 +950,7 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
     STRACE(trace_base + 2);
   }
   after_stream(ring);
+  if constexpr (SCALES_LOADED) cp_async_wait_all();  // the scales copied before the dependency wait
 
   // ---- combine: the warps' partials in warp order, then finish each tile
   __syncthreads();
@@ -1028,7 +1035,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_streamk_kernel(const __grid_
     const int u0 = range_start(p, blockIdx.x), u1 = range_start(p, blockIdx.x + 1);
     if (u1 > u0) {
       const int vt_first = fdiv(u0, p.div_kbpv);
-      load_scales<P>(p, io_of_params(p), epi_of(p, smem, P), vt_first, fdiv(u1 - 1, p.div_kbpv) - vt_first + 1, tid);
+      load_scales<P, true>(p, io_of_params(p), epi_of(p, smem, P), vt_first, fdiv(u1 - 1, p.div_kbpv) - vt_first + 1,
+                           tid);
     }
   }
   pdl_wait();
