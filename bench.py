@@ -839,6 +839,81 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# --timeline: where each launch of the decode step spends its time
+# ---------------------------------------------------------------------------
+TRACE_LIB = PKG_DIR / "libb200gemv_trace.so"
+PHASES = ("start", "waited", "staged", "streamed", "end")
+
+
+def run_timeline(args):
+    """Per-CTA phase timestamps (%globaltimer) of every launch of one graph
+    replay of the stack, from the trace build of the library (B2G_TRACE;
+    built next to the library if missing).  Points: 0 start, 1 past the
+    dependency wait, 2 inputs staged (after the CTA barrier), 3 this warp's
+    weights streamed (thread 0), 4 end.  Prints one JSON line per M: per
+    kernel, the means over the middle layers of each phase's median over
+    CTAs, and of the critical-path marks measured from the launch's first
+    release (its earliest CTA past the wait)."""
+    import ctypes
+    import torch
+    build = load_module("b2g_build", PKG_DIR / "build.py")
+    if not TRACE_LIB.exists():
+        build.build(force=True, out=TRACE_LIB, defines=["B2G_TRACE"])
+    b2g = load_module("b2g", PKG_DIR / "__init__.py", package=True)
+    b2g.LIB_PATH = TRACE_LIB
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    st = b2g.Stack(HIDDEN, INTER, LAYERS, max_m=8)
+    layers = make_layers(b2g, torch, device, 1, 0, (st.gate_up, st.down), 8)
+    for i, L in enumerate(layers):
+        st.set_layer(i, L["pgu"], L["sgu"], L["pd"], L["sd"])
+    ws = torch.zeros(max(st.gate_up.workspace_bytes(), st.down.workspace_bytes()), dtype=torch.uint8, device=device)
+    lib = ctypes.CDLL(str(TRACE_LIB))
+    n_launch, n_cta = 64, 160
+    grids = (st.gate_up.plan(8)["grid"], st.down.plan(8)["grid"])
+    for M in sorted({args.m, 1}, reverse=True):
+        h = torch.randn(M, HIDDEN, device=device).half()
+        act = torch.empty(M, INTER, device=device, dtype=torch.float16)
+        g = _graph_of(torch, lambda: st.enqueue(h, act, ws))
+        for _ in range(5):
+            g.replay()
+        torch.cuda.synchronize()
+        buf = np.zeros((n_launch, n_cta, 8), dtype=np.uint64)
+        if lib.b2g_debug_trace(ctypes.c_void_p(buf.ctypes.data), ctypes.c_size_t(buf.nbytes)) != 0:
+            raise RuntimeError("b2g_debug_trace failed")
+        g.reset()
+        nl = 2 * LAYERS
+        order = np.argsort(buf[:, 0, 0].astype(np.int64))[-nl:]  # the last replay's launches, in time order
+        rows = []
+        for i, slot in enumerate(order):
+            t = buf[slot, :grids[i % 2], :5].astype(np.int64)
+            rows.append({k: (int(t[:, j].min()), int(np.median(t[:, j])), int(t[:, j].max()))
+                         for j, k in enumerate(PHASES)})
+        mid = range(4, nl - 4)
+
+        def mean(kind, f):
+            return round(float(np.mean([f(i) for i in mid if i % 2 == kind])) / 1e3, 3)
+        out = {"timeline": "stack per-layer mode, one graph replay", "m": M, "layers": LAYERS,
+               "us_per_layer": round((rows[nl - 4]["waited"][0] - rows[4]["waited"][0]) / ((nl - 8) / 2) / 1e3, 3)}
+        for kind, name in ((0, "gate_up"), (1, "down")):
+            out[name] = {
+                "grid": grids[kind],
+                "release_after_previous_last_end": mean(kind, lambda i: rows[i]["waited"][0] - rows[i - 1]["end"][2]),
+                "wait_exit_spread": mean(kind, lambda i: rows[i]["waited"][2] - rows[i]["waited"][0]),
+                "staging_median": mean(kind, lambda i: rows[i]["staged"][1] - rows[i]["waited"][1]),
+                "stream_median": mean(kind, lambda i: rows[i]["streamed"][1] - rows[i]["staged"][1]),
+                "epilogue_median": mean(kind, lambda i: rows[i]["end"][1] - rows[i]["streamed"][1]),
+                "last_staged_after_release": mean(kind, lambda i: rows[i]["staged"][2] - rows[i]["waited"][0]),
+                "last_streamed_after_release": mean(kind, lambda i: rows[i]["streamed"][2] - rows[i]["waited"][0]),
+                "last_end_after_release": mean(kind, lambda i: rows[i]["end"][2] - rows[i]["waited"][0]),
+            }
+        print(json.dumps(out), flush=True)
+    err = b2g.device_error()
+    if err:
+        raise RuntimeError(f"device error {err}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -860,6 +935,8 @@ def main():
                     help="how the GEMV launches feed their weights (B2G_OPT_PIPE)")
     ap.add_argument("--stack-mode", choices=["per_layer", "persistent", "persistent_tma"], default="per_layer",
                     help="one GPU: the stack's execution mode for the timed step")
+    ap.add_argument("--timeline", action="store_true",
+                    help="one GPU: per-phase timestamps of the stack's launches (trace build), not the bench line")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decode-MLP layers (28 = Llama-3.2-3B; fewer only for small profiling captures)")
     args = ap.parse_args()
@@ -868,6 +945,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.timeline:
+        run_timeline(args)
     else:
         run_ours(args)
 

@@ -8,6 +8,7 @@
 // partition, pipeline depth and shared-memory layout from the shape and the
 // device (SM count, shared memory per block).
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -55,6 +56,9 @@ b2g_status cuda_status(cudaError_t e) { return e == cudaSuccess ? B2G_OK : B2G_E
 std::mutex g_mu;
 bool g_limit_set[64];
 int* g_err_word[64];
+// Launches enqueued so far (a trace build files each launch's phase
+// timestamps under this count).
+std::atomic<unsigned> g_launch_count{0};
 
 // L2 prefetch depth: the first bytes of each next-launch CTA's range that a
 // launch warms (the start is what the next CTA's register ring asks for
@@ -556,6 +560,7 @@ static b2g_status enqueue_impl(const b2g_op* op, const b2g_enqueue_args* a, cons
     p.pf_bytes = use_tma(op, lp) ? kPrefetchBytesTma : kPrefetchBytesPerCta;
   }
   if (tp) p.tp = *tp;
+  p.trace_slot = (int)(g_launch_count.fetch_add(1, std::memory_order_relaxed) & 0x3fffffff);
   // One contributor per output tile (no K split, no tile shared between
   // CTAs) and aligned rows: the lean kernel flavor.
   p.lean = op->ksplit == 1 && op->max_contrib == 1 && aligned(a->x, 16) && a->ldx % 8 == 0 && op->K % 32 == 0;

@@ -48,12 +48,19 @@ namespace b2g {
 __device__ int g_device_error;
 
 #ifdef B2G_TRACE
-// Per-CTA phase timestamps (%globaltimer), debug builds only.  g_trace: the
-// single-op kernel's points; g_strace: 4 points per stack phase.
+// Per-CTA phase timestamps (%globaltimer), trace builds only.  g_tl: the
+// single-op kernels' points 0 start, 1 past the dependency wait, 2 inputs
+// staged, 3 weights streamed, 4 end, per launch slot (the host's launch
+// count mod kTraceLaunches) and CTA; g_strace: 4 points per stack phase.
 constexpr int kTracePts = 256;
-__device__ unsigned long long g_trace[1024][16];
+constexpr int kTraceLaunches = 64;
+constexpr int kTraceCtas = 160;
+__device__ unsigned long long g_tl[kTraceLaunches][kTraceCtas][8];
 __device__ unsigned long long g_strace[160][kTracePts];
-#define TRACE(i) do { g_trace[blockIdx.x][(i)] = globaltimer_ns(); } while (0)
+#define TRACE(i) \
+  do { \
+    if (blockIdx.x < kTraceCtas) g_tl[p.trace_slot % kTraceLaunches][blockIdx.x][(i)] = globaltimer_ns(); \
+  } while (0)
 #define STRACE(i) \
   do { if ((i) >= 0 && (i) < kTracePts && blockIdx.x < 160) g_strace[blockIdx.x][(i)] = globaltimer_ns(); } while (0)
 #else
@@ -1430,7 +1437,6 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
   const unsigned G = gridDim.x;
   uint4 ring[R];
   unsigned nbar = 0;
-  if (tid == 0) TRACE(0);
   l2_prefetch_phase(gu, sp.layers[0].pgu, 2 * kUnitPlaneBytes, kWholeRange);
   prefetch_phase<2, R>(gu, sp.layers[0].pgu, ring, warp, lane, pol);
   for (int l = 0; l < sp.n_layers; ++l) {
@@ -1456,7 +1462,6 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
     }
   }
   grid_exit(sp.barrier, (nbar + 1) * G);
-  if (tid == 0) TRACE(4);
 }
 
 
@@ -1702,8 +1707,11 @@ cudaError_t launch_tp_gather(const TpParams& tp, int m, int* error, cudaStream_t
 }
 
 #ifdef B2G_TRACE
-extern "C" int b2g_debug_trace(unsigned long long* out, int n_ctas) {
-  return (int)cudaMemcpyFromSymbol(out, g_trace, sizeof(unsigned long long) * 16 * n_ctas);
+// The whole per-launch timeline: [kTraceLaunches][kTraceCtas][8] u64 (bytes
+// must be at least its size).
+extern "C" int b2g_debug_trace(unsigned long long* out, size_t bytes) {
+  if (bytes < sizeof(g_tl)) return (int)cudaErrorInvalidValue;
+  return (int)cudaMemcpyFromSymbol(out, g_tl, sizeof(g_tl));
 }
 extern "C" int b2g_debug_stack_trace(unsigned long long* out, int n_ctas) {
   return (int)cudaMemcpyFromSymbol(out, g_strace, sizeof(unsigned long long) * kTracePts * n_ctas);

@@ -153,6 +153,7 @@ struct GemvParams {
   int pf_grid;
   int pf_bytes;
   TpParams tp;
+  int trace_slot;  // trace builds: this launch's slot in the per-launch timeline
 };
 
 // Final gather of a tensor-parallel chain: h = sum of the inbox slots once
