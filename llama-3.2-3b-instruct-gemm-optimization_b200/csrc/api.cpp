@@ -62,11 +62,14 @@ std::atomic<unsigned> g_launch_count{0};
 
 // L2 prefetch depth: the first bytes of each next-launch CTA's range that a
 // launch warms (the start is what the next CTA's register ring asks for
-// first; warming whole ranges moves more of the next launch's HBM traffic
-// into this launch's window).  Per decode layer (gate||up on 128 CTAs, down
-// on 96): 64 KB 26.2 us, 128 KB 26.5, 256 KB 25.9, whole ranges 26.1 at
-// M = 8; 25.3 / 25.7 / 24.4 / 24.5 at M = 1.
+// first).  The fills compete with the launch's own critical path (its late
+// CTAs' first loads, the activation staging), so deeper is not better.  Per
+// decode layer (gate||up on 128 CTAs, down on 96), 128 / 256 / 512 KB:
+// M = 8 20.29 / 20.12 / 20.88 us; M = 1 18.90 / 19.34 / 19.60.  With
+// 128 KB up to M = 4 and 256 KB above: M = 1 / 2 / 4 / 8 18.91 / 19.41 /
+// 19.77 / 20.11 against 19.27 / 19.64 / 19.81 / 20.12 with 256 KB at all M.
 constexpr int kPrefetchBytesPerCta = 256 * 1024;
+constexpr int kPrefetchBytesSmallM = 128 * 1024;  // M <= 4
 // The TMA pipeline issues its prefetch once its own copies are all issued,
 // and asks for whole ranges (the next launch then streams from L2).
 constexpr int kPrefetchBytesTma = 1 << 30;
@@ -557,7 +560,7 @@ static b2g_status enqueue_impl(const b2g_op* op, const b2g_enqueue_args* a, cons
     p.pf_gran = nx->gran;
     p.pf_unit_bytes = nx->unit_bytes;
     p.pf_grid = nx->grid;
-    p.pf_bytes = use_tma(op, lp) ? kPrefetchBytesTma : kPrefetchBytesPerCta;
+    p.pf_bytes = use_tma(op, lp) ? kPrefetchBytesTma : a->m <= 4 ? kPrefetchBytesSmallM : kPrefetchBytesPerCta;
   }
   if (tp) p.tp = *tp;
   p.trace_slot = (int)(g_launch_count.fetch_add(1, std::memory_order_relaxed) & 0x3fffffff);
