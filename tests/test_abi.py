@@ -133,3 +133,28 @@ int main(void) {{
     assert out[0].startswith("version ") and out[0].endswith(f"entries {len(declared_functions())}")
     assert out[1] == f"3072 8192 128 2 {2 * 3072 * 8192}"
     assert out[2] == f"8192 3072 96 2 {8192 * 3072}"
+
+
+@pytest.mark.parametrize("world,max_m,width", [(1, 8, 256), (2, 8, 3072), (8, 8, 3072), (4, 1, 3072)])
+def test_tp_comm_layout_without_a_device(b2g, world, max_m, width):
+    """The exchange buffer's layout is arithmetic on the base address: the
+    inbox first (big enough for the REDUCE words, [2][world][max_m][width/2]
+    x 8 B, which also covers the fp16 PUSH slots), then the 256-byte counter
+    region, then the epoch region with the per-CTA round counts (word 64
+    on, B2G_TP_MAX_CTAS of them); every region 256-byte aligned."""
+    n = b2g.tp_comm_bytes(world, max_m, width)
+    inbox_bytes = -(-2 * world * max_m * (width // 2) * 8 // 256) * 256
+    epoch_bytes = -(-(64 + b2g.TP_MAX_CTAS) * 4 // 256) * 256
+    assert n == inbox_bytes + 256 + epoch_bytes
+    base = 1 << 40  # never dereferenced
+    inbox, counters, epoch = b2g.tp_comm_layout(base, world, max_m, width)
+    assert (inbox, counters, epoch) == (base, base + inbox_bytes, base + inbox_bytes + 256)
+    assert epoch + (64 + b2g.TP_MAX_CTAS) * 4 <= base + n
+    assert 2 * world * max_m * width * 2 <= inbox_bytes  # the fp16 slots fit as well
+
+
+@pytest.mark.parametrize("world,max_m,width", [(0, 8, 256), (9, 8, 256), (2, 0, 256), (2, 8, 4)])
+def test_tp_comm_rejects_bad_sizes(b2g, world, max_m, width):
+    assert b2g.tp_comm_bytes(world, max_m, width) == 0
+    with pytest.raises(b2g.B2GError):
+        b2g.tp_comm_layout(1 << 40, world, max_m, width)
