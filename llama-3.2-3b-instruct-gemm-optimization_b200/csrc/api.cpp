@@ -65,11 +65,15 @@ std::atomic<unsigned> g_launch_count{0};
 // first).  The fills compete with the launch's own critical path (its late
 // CTAs' first loads, the activation staging), so deeper is not better.  Per
 // decode layer (gate||up on 128 CTAs, down on 96), 128 / 256 / 512 KB:
-// M = 8 20.29 / 20.12 / 20.88 us; M = 1 18.90 / 19.34 / 19.60.  With
-// 128 KB up to M = 4 and 256 KB above: M = 1 / 2 / 4 / 8 18.91 / 19.41 /
-// 19.77 / 20.11 against 19.27 / 19.64 / 19.81 / 20.12 with 256 KB at all M.
+// M = 8 20.29 / 20.12 / 20.88 us; M = 1 18.90 / 19.34 / 19.60.  What pays
+// at small M is warming less of a fused gate||up launch (393 KB per CTA)
+// while the down launch runs; down's own 256 KB ranges are best warmed
+// whole.  128 KB for a next gate||up launch up to M = 4, 256 KB otherwise:
+// M = 1 / 2 / 4 / 8 18.69 / 19.19 / 19.57 / 20.10 us, against 19.27 /
+// 19.64 / 19.81 / 20.12 with 256 KB everywhere, and a chain of down GEMVs
+// at M = 1 keeps its 7.13 us (7.84 with 128 KB).
 constexpr int kPrefetchBytesPerCta = 256 * 1024;
-constexpr int kPrefetchBytesSmallM = 128 * 1024;  // M <= 4
+constexpr int kPrefetchBytesSmallM = 128 * 1024;  // a next two-plane launch at M <= 4
 // The TMA pipeline issues its prefetch once its own copies are all issued,
 // and asks for whole ranges (the next launch then streams from L2).
 constexpr int kPrefetchBytesTma = 1 << 30;
@@ -560,7 +564,9 @@ static b2g_status enqueue_impl(const b2g_op* op, const b2g_enqueue_args* a, cons
     p.pf_gran = nx->gran;
     p.pf_unit_bytes = nx->unit_bytes;
     p.pf_grid = nx->grid;
-    p.pf_bytes = use_tma(op, lp) ? kPrefetchBytesTma : a->m <= 4 ? kPrefetchBytesSmallM : kPrefetchBytesPerCta;
+    p.pf_bytes = use_tma(op, lp)                  ? kPrefetchBytesTma
+                 : (a->m <= 4 && nx->planes == 2) ? kPrefetchBytesSmallM
+                                                  : kPrefetchBytesPerCta;
   }
   if (tp) p.tp = *tp;
   p.trace_slot = (int)(g_launch_count.fetch_add(1, std::memory_order_relaxed) & 0x3fffffff);
