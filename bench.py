@@ -258,7 +258,7 @@ def per_config(b2g, torch, device, layers, hbm: float, ms: tuple, reps: int = 5)
             us = _chain_us(torch, [mk(i) for i in range(LAYERS)], reps)
             rec(f"{name}_m{M}", K, N, M, us, gemv_bytes(K, N, M, 1, 4), grid=op.plan(M)["grid"])
         if 8 in ms:
-            # north-star item: CUDA-core FFMA against mma.sync at M = 8
+            # the CUDA-core FFMA variant against the tensor-core path at M = 8
             op.set_option(b2g.OPT_MATH, b2g.MATH_FFMA)
             x = xs[8][:, :K].contiguous()
             us = _chain_us(torch, [(lambda i=i: op.enqueue(x, packs[i], scales[i], y=y[:8, :N], workspace=ws, pdl=True,

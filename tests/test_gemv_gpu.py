@@ -1,6 +1,6 @@
 """GPU parity: the CUDA path (through the C ABI) against the CPU oracle.
 
-Tolerances (north star): rel-L2 <= 1e-3 for FP16 weights and <= 5e-3 for
+Tolerances: rel-L2 <= 1e-3 for FP16 weights and <= 5e-3 for
 E4M3 weights, measured against the fp64 oracle over the same quantised bytes
 and scales; max-abs is asserted against a stated bound as well.  Quantisation
 itself is bit-exact.  The reference's own acceptance gates are checked on its
