@@ -467,6 +467,8 @@ def run_ours(args):
     pipe = {"auto": b2g.PIPE_AUTO, "registers": b2g.PIPE_REGISTERS, "tma": b2g.PIPE_TMA}[args.pipe]
     for op in (gu_op, dn_op):
         op.set_option(b2g.OPT_PIPE, pipe)
+        if args.math == "ffma":
+            op.set_option(b2g.OPT_MATH, b2g.MATH_FFMA)
     if st is not None and args.stack_mode != "per_layer":
         st.set_mode(args.stack_mode)
     want_ref = tp == 1 and not args.no_ref_kernels and REF_GPU_LIB.exists()
@@ -611,7 +613,7 @@ def run_ours(args):
     # the gate||up launch carries the exchange only when it gathers the rows itself
     exch = 1 if tp > 1 and tps.fused and tps.exchange == "gather_launch" else 0
     gu_kernel = (f"gemv_tma_kernel<2,1,{exch}>" if gu_plan["pipe"] == b2g.PIPE_TMA
-                 else f"gemv_streamk_kernel<2,1,0,{3 if exch else 0}>")
+                 else f"gemv_streamk_kernel<2,1,{gu_plan['math']},{3 if exch else 0}>")
     roofline = {"kernel": f"{gu_kernel} (RMSNorm + gate||up + SiLU*up)",
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "traffic": traffic,
@@ -933,6 +935,8 @@ def main():
                     help="N > 1, fused: how the ranks' rows are summed (TPStack.exchange)")
     ap.add_argument("--pipe", choices=["auto", "registers", "tma"], default="auto",
                     help="how the GEMV launches feed their weights (B2G_OPT_PIPE)")
+    ap.add_argument("--math", choices=["mma", "ffma"], default="mma",
+                    help="the GEMV launches' math: tensor-core mma.sync, or the CUDA-core FFMA variant (B2G_OPT_MATH)")
     ap.add_argument("--stack-mode", choices=["per_layer", "persistent", "persistent_tma"], default="per_layer",
                     help="one GPU: the stack's execution mode for the timed step")
     ap.add_argument("--timeline", action="store_true",
