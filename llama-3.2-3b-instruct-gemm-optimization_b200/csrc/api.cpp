@@ -572,7 +572,9 @@ static b2g_status enqueue_impl(const b2g_op* op, const b2g_enqueue_args* a, cons
   p.trace_slot = (int)(g_launch_count.fetch_add(1, std::memory_order_relaxed) & 0x3fffffff);
   // One contributor per output tile (no K split, no tile shared between
   // CTAs) and aligned rows: the lean kernel flavor.
-  p.lean = op->ksplit == 1 && op->max_contrib == 1 && aligned(a->x, 16) && a->ldx % 8 == 0 && op->K % 32 == 0;
+  const bool resid = (op->f.fuse & B2G_FUSE_RESIDUAL_ADD) != 0;
+  p.lean = op->ksplit == 1 && op->max_contrib == 1 && aligned(a->x, 16) && a->ldx % 8 == 0 && op->K % 32 == 0 &&
+           (!resid || (aligned(a->residual, 16) && a->ldr % 8 == 0));
   if (tp && tp->mode == kTpReduce) {
     // The REDUCE flavor is the lean one: whole tiles, aligned rows; y takes
     // 4-byte pieces; one round count per CTA; register pipeline only.

@@ -214,6 +214,16 @@ __device__ __forceinline__ void cp_async4(void* smem_dst, const void* src) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// 16 bytes global -> shared through L2 only (the source may have been
+// written by another SM since this one last read it); both addresses
+// 16-byte aligned.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(src)
+               : "memory");
+}
+
 // float -> E4M3 code, round to nearest even, saturate to +-448.
 __device__ __forceinline__ uint8_t f32_to_e4m3(float f) {
   uint16_t r;

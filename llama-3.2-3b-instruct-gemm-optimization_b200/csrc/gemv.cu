@@ -139,12 +139,12 @@ __device__ __forceinline__ float2 h2_to_f2(uint32_t v) {
 // the residual rows.  Slot j is the CTA's j-th virtual tile.
 struct Epi {
   float* scale;  // [n_slots][P][16]
-  float* res;    // [n_slots][8][16]
+  __half* res;   // [n_slots][8][16], as stored in memory
 };
 
 __device__ __forceinline__ Epi epi_of(const GemvParams& p, uint8_t* smem, int P) {
   float* base = reinterpret_cast<float*>(smem + p.off_epi);
-  return Epi{base, base + p.n_slots * P * 16};
+  return Epi{base, reinterpret_cast<__half*>(base + p.n_slots * P * 16)};
 }
 
 // The scales of the CTA's tiles (constants: may load before the previous
@@ -177,7 +177,32 @@ __device__ __forceinline__ void load_residual(const GemvParams& p, const Io& io,
       const int j = i / 128, m = (i / 16) % 8, c = i % 16;
       const int vt = vt_first + j;
       const int n = (vt - fdiv(vt, p.div_tiles) * p.n_tiles) * kTileCh + c;
-      e.res[i] = (m < p.M && n < p.N) ? __half2float(__ldcg(io.residual + (size_t)m * io.ldr + n)) : 0.f;
+      e.res[i] = (m < p.M && n < p.N) ? __ldcg(io.residual + (size_t)m * io.ldr + n) : __float2half(0.f);
+    }
+  }
+}
+
+// The same rows without stalling a thread: 16-byte pieces (8 channels of one
+// row of a tile) global -> shared with cp.async, issued before the
+// activations are staged so that the two round trips overlap; a piece that
+// would cross N goes element by element.  Rows are 16-byte aligned (lean
+// flavor, host-checked); the caller completes the copies before the epilogue.
+template <int P>
+__device__ __forceinline__ void load_residual_async(const GemvParams& p, const Io& io, const Epi& e, int vt_first,
+                                                    int nvt, int tid) {
+  if (P == 1 && p.residual_add) {
+    const int np = nvt * p.M * 2;
+    for (int i = tid; i < np; i += NT) {
+      const int j = i / (p.M * 2), r = i - j * (p.M * 2), m = r >> 1, h = r & 1;
+      const int vt = vt_first + j;
+      const int n0 = (vt - fdiv(vt, p.div_tiles) * p.n_tiles) * kTileCh + h * 8;
+      __half* dst = e.res + (j * 8 + m) * 16 + h * 8;
+      const __half* src = io.residual + (size_t)m * io.ldr + n0;
+      if (n0 + 8 <= p.N) {
+        cp_async16(dst, src);
+      } else {
+        for (int c = 0; c < 8; ++c) dst[c] = n0 + c < p.N ? __ldcg(src + c) : __float2half(0.f);
+      }
     }
   }
 }
@@ -198,7 +223,7 @@ __device__ __forceinline__ void load_epi(const GemvParams& p, const Io& io, cons
       const int j = i / 128, m = (i / 16) % 8, c = i % 16;
       const int vt = vt_first + j;
       const int n = (vt - fdiv(vt, p.div_tiles) * p.n_tiles) * kTileCh + c;
-      e.res[i] = (m < p.M && n < p.N) ? __half2float(__ldcg(io.residual + (size_t)m * io.ldr + n)) : 0.f;
+      e.res[i] = (m < p.M && n < p.N) ? __ldcg(io.residual + (size_t)m * io.ldr + n) : __float2half(0.f);
     }
   }
 }
@@ -257,7 +282,7 @@ __device__ __forceinline__ void epilogue(const GemvParams& p, const Io& io, int 
       __half out;
       if constexpr (P == 1) {
         out = __float2half_rn(v[0][i] * r * e.scale[j * 16 + c]);
-        if (p.residual_add) out = __float2half_rn(e.res[(j * 8 + m) * 16 + c] + __half2float(out));
+        if (p.residual_add) out = __float2half_rn(__half2float(e.res[(j * 8 + m) * 16 + c]) + __half2float(out));
       } else {
         const float gf = __half2float(__float2half_rn(v[0][i] * r * e.scale[(j * 2) * 16 + c]));
         const float uf = __half2float(__float2half_rn(v[1][i] * r * e.scale[(j * 2 + 1) * 16 + c]));
@@ -863,11 +888,12 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
              reinterpret_cast<volatile int*>(smem + kOffMisc), [] { __syncthreads(); });
   }
   if (active) {
+    if (LEAN && SCALES_LOADED) load_residual_async<P>(p, io, epi, vt_first, vt_last - vt_first + 1, tid);
     if (!gather) stage_x<LEAN>(p, io, xs, k_lo, krange, tid, p.rmsnorm ? red : nullptr);
-    if (SCALES_LOADED)
-      load_residual<P>(p, io, epi, vt_first, vt_last - vt_first + 1, tid);
-    else
+    if (!SCALES_LOADED)
       load_epi<P>(p, io, epi, vt_first, vt_last - vt_first + 1, tid);
+    else if (!LEAN)
+      load_residual<P>(p, io, epi, vt_first, vt_last - vt_first + 1, tid);
   }
   for (int i = tid; i < p.n_slots * W * P * 32; i += NT) slots[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   __syncthreads();
@@ -957,7 +983,7 @@ __device__ __forceinline__ void run_phase(const GemvParams& p, const Io& io, uin
     STRACE(trace_base + 2);
   }
   after_stream(ring);
-  if constexpr (SCALES_LOADED) cp_async_wait_all();  // the scales copied before the dependency wait
+  if constexpr (SCALES_LOADED) cp_async_wait_all();  // the scales (and lean residual rows) copied asynchronously
 
   // ---- combine: the warps' partials in warp order, then finish each tile
   __syncthreads();
