@@ -693,7 +693,8 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
-            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            # tensor parallel over one fixed workload at every N: strong scaling
+            "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp8_e4m3", "data": "synthetic",
             "config": {
                 "workload": (f"{LAYERS}-layer Llama-3.2-3B decode MLP stack, M={M}: RMSNorm(eps 1e-5) -> "
